@@ -1,0 +1,378 @@
+"""Benchmark of the tensor-ring operator on B200 -- one JSON line on rank 0.
+
+Workload (BASELINE metric): CUDA-event microseconds per call of the fused operator on the
+1920->2880 ring, modes (8,12,20)->(12,10,24), fp16, at R=8 with T=1/8/32 and at R=16 with
+T=1/32, next to cuBLAS dense fp16 GEMM of the same (d_in, d_out).  Synthetic, seeded: cores
+N(0, sigma^2) with sigma = (R*d_in^(1/3))^(-1/2), x ~ N(0,1).
+
+Per case:
+  value leg   one call per step, L2 flushed (256 MiB write) before every step, CUDA events
+              around the call on the launching stream: device time of a cold-cache call.
+  warm leg    the reference harness's protocol: 5 blocks x 20 back-to-back calls, median
+              (benchmarks/benchmark.py:163-174), reported beside the H100 figures.
+  e2e leg     the public API end to end: pinned host x -> device, fn(x), y -> pinned host,
+              after an L2 flush and with the GPU idle, so host dispatch is inside the region.
+  dense bar   F.linear(x, W) on the materialised fp16 W, same legs (TF32 off).
+value = mean over the five cases of the median value-leg time.  ms_per_step = one call of each
+case.  --impl reference times the reference's CPU path (the numpy restatement in oracle/) on the
+host cores instead.  Under torchrun (N>1) every rank serves its own replica of the suite
+(tokens are independent, no collective on the data path); times are the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import platform
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = ("CUDA-event µs/call at T=1/8/32 (r8), T=1/32 (r16) vs cuBLAS dense fp16 GEMM")
+CASES = [(8, 1), (8, 8), (8, 32), (16, 1), (16, 32)]
+H100_PUBLISHED = {(8, 1): 8.2, (8, 8): 12.3, (8, 32): 27.9, (16, 1): 10.7, (16, 32): 82.4}
+FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-dense", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={index}", f"--query-gpu={self.Q}", "--format=csv,noheader",
+                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.file.read().splitlines():
+            f = [v.strip() for v in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1].split()[0]))
+                smax.append(float(f[2].split()[0]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.file.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dense_weight(cores):
+    """The equivalent dense W [d_out, d_in] (the performance bar only; fp32 accumulate)."""
+    A, B, C = (c.float() for c in cores)
+    part = torch.einsum("apib,bqjc->apiqjc", A, B)
+    W = torch.einsum("apiqjc,crka->pqrijk", part, C)
+    P, Q, Rr, ni, nj, nk = W.shape
+    return W.reshape(P * Q * Rr, ni * nj * nk).to(cores[0].dtype)
+
+
+def cold_device_us(fn, x, flush, steps, warmup):
+    """Per-call device time with L2 flushed before every call (flush outside the events)."""
+    for _ in range(warmup):
+        flush.add_(1)
+        fn(x)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    for s, e in evs:
+        flush.add_(1)
+        s.record()
+        fn(x)
+        e.record()
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) * 1e3 for s, e in evs]
+
+
+def warm_stream_us(fn, x, blocks=5, per_block=20):
+    for _ in range(20):
+        fn(x)
+    out = []
+    for _ in range(blocks):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(per_block):
+            fn(x)
+        e.record()
+        e.synchronize()
+        out.append(s.elapsed_time(e) * 1e3 / per_block)
+    return statistics.median(out)
+
+
+def e2e_us(fn, x_host, flush, steps, warmup, d_out):
+    """Public API end to end: pinned x -> device, fn, y -> pinned host, GPU idle at start."""
+    dev = flush.device
+    x_dev = torch.empty(x_host.shape, dtype=x_host.dtype, device=dev)
+    y_host = torch.empty((x_host.shape[0], d_out), dtype=x_host.dtype, pin_memory=True)
+    res = []
+    for i in range(warmup + steps):
+        flush.add_(1)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        x_dev.copy_(x_host, non_blocking=True)
+        y = fn(x_dev)
+        y_host.copy_(y, non_blocking=True)
+        e.record()
+        e.synchronize()
+        if i >= warmup:
+            res.append(s.elapsed_time(e) * 1e3)
+    return res, x_host.numel() * x_host.element_size(), y_host.numel() * y_host.element_size()
+
+
+def host_latency_us(fn, x, n=100):
+    lat = []
+    for _ in range(n):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        fn(x)
+        torch.cuda.synchronize()
+        lat.append((time.perf_counter() - t0) * 1e6)
+    return statistics.median(lat)
+
+
+def max_over_ranks(vals, world):
+    if world == 1:
+        return vals
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return t.tolist()
+
+
+def cpu_reference_leg(steps_budget_s=2.0):
+    """The reference's CPU contraction (numpy restatement, fp32, all host threads) per case."""
+    import oracle
+    from kernel_task_b200.spec import TRSpec, baseline_cores, baseline_x
+
+    threads = os.cpu_count() or 1
+    per_case = {}
+    for R, T in CASES:
+        spec = TRSpec((8, 12, 20), (12, 10, 24), R)
+        cores = [c.float().numpy() for c in baseline_cores(spec, seed=0)]
+        x = baseline_x(spec, T, seed=0).float().numpy()
+        oracle.tr_forward_reference(x, cores)
+        lat, t_end = [], time.perf_counter() + steps_budget_s
+        while time.perf_counter() < t_end or len(lat) < 3:
+            t0 = time.perf_counter()
+            oracle.tr_forward_reference(x, cores)
+            lat.append((time.perf_counter() - t0) * 1e6)
+        per_case[f"r{R}_t{T}"] = {"us": statistics.median(lat), "calls": len(lat)}
+    value = statistics.mean(v["us"] for v in per_case.values())
+    return value, threads, per_case
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    value, threads, per_case = cpu_reference_leg()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "us/call",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(sum(v["us"] for v in per_case.values()) / 1e3, 4),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,sigma^2) cores, N(0,1) x)",
+        "config": {"workload": "c1+c2 decode suite: 1920->2880 (8,12,20)->(12,10,24), "
+                               "R8 T=1/8/32 and R16 T=1/32", "cases": per_case},
+        "cpu_baseline": {"value": round(value, 2), "unit": "us/call", "cores": threads,
+                         "kind": "port", "sample": "each of the 5 cases, repeated calls for "
+                         "~2 s, median; numpy fp32 restatement of tr_forward_reference"},
+        "e2e": {"value": round(value, 2), "unit": "us/call", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "cpu": platform.processor() or platform.machine(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local_rank):
+    from kernel_task_b200 import prepare_optimized
+    from kernel_task_b200.spec import TRSpec, baseline_cores, baseline_x
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    hbm_peak, tc_peak, peak_kind = peaks()
+    steps, warmup = args.steps, max(3, args.warmup)
+
+    cases = {}
+    for R, T in CASES:
+        spec = TRSpec((8, 12, 20), (12, 10, 24), R)
+        cores = baseline_cores(spec, seed=0, dtype=torch.float16, device=dev)
+        x = baseline_x(spec, T, seed=0, dtype=torch.float16, device=dev)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        fn = prepare_optimized(cores, spec)
+        torch.cuda.synchronize()
+        prep_ms = (time.perf_counter() - t0) * 1e3
+        cases[(R, T)] = {"spec": spec, "cores": cores, "x": x, "fn": fn, "prep_ms": prep_ms}
+
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ
+                    else int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank]))
+    launches = 0
+    for key, c in cases.items():
+        c["cold"] = cold_device_us(c["fn"], c["x"], flush, steps, warmup)
+        launches += steps
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clk = clocks.stop()
+
+    for key, c in cases.items():
+        c["warm"] = warm_stream_us(c["fn"], c["x"])
+        c["host"] = host_latency_us(c["fn"], c["x"])
+        xh = c["x"].cpu().pin_memory()
+        e2e, c["h2d"], c["d2h"] = e2e_us(c["fn"], xh, flush, steps, warmup,
+                                          c["spec"].out_features)
+        c["e2e"] = e2e
+        if not args.no_dense:
+            W = dense_weight(c["cores"])
+            dfn = lambda v, W=W: torch.nn.functional.linear(v, W)  # noqa: E731
+            c["dense_cold"] = statistics.median(cold_device_us(dfn, c["x"], flush, steps,
+                                                               warmup))
+            c["dense_warm"] = warm_stream_us(dfn, c["x"])
+            c["dense_e2e"] = statistics.median(e2e_us(dfn, xh, flush, steps, warmup,
+                                                      c["spec"].out_features)[0])
+            del W
+        c["flops"] = c["fn"].flops_per_token() * c["x"].shape[0]
+        c["tiling"] = c["fn"].tiling(c["x"].shape[0])
+
+    keys = list(cases)
+    med = max_over_ranks([statistics.median(cases[k]["cold"]) for k in keys], world)
+    mean = max_over_ranks([statistics.mean(cases[k]["cold"]) for k in keys], world)
+    e2e = max_over_ranks([statistics.median(cases[k]["e2e"]) for k in keys], world)
+    if rank != 0:
+        return
+    per_case = {}
+    for i, k in enumerate(keys):
+        c = cases[k]
+        R, T = k
+        spec = c["spec"]
+        bytes_min = 2 * (spec.factor_parameters + T * (spec.in_features + spec.out_features))
+        per_case[f"r{R}_t{T}"] = {
+            "us": round(med[i], 3), "us_mean": round(mean[i], 3),
+            "warm_stream_us": round(c["warm"], 3), "host_latency_us": round(c["host"], 2),
+            "e2e_us": round(e2e[i], 3), "prep_ms": round(c["prep_ms"], 2),
+            "dense_us": round(c.get("dense_cold", float("nan")), 3),
+            "dense_warm_stream_us": round(c.get("dense_warm", float("nan")), 3),
+            "dense_e2e_us": round(c.get("dense_e2e", float("nan")), 3),
+            "h100_published_warm_stream_us": H100_PUBLISHED[k],
+            "flops": c["flops"], "min_bytes": bytes_min,
+            "tflops": round(c["flops"] / (mean[i] * 1e-6) / 1e12, 2),
+            "tiling": c["tiling"], "packed_bytes": int(c["fn"].packed.numel()),
+            "workspace_bytes": int(c["fn"].workspace_bytes(T)),
+        }
+    # roofline of the dominant kernel: the case with the largest device time
+    dom = max(range(len(keys)), key=lambda i: mean[i])
+    dk = keys[dom]
+    achieved = cases[dk]["flops"] / (mean[dom] * 1e-6) / 1e12
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(f"r{dk[0]}_t{dk[1]}")
+    value = statistics.mean(med)
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "us/call", "n_gpus": world,
+        "steps": steps, "warmup": warmup, "ms_per_step": round(sum(med) / 1e3, 5),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded N(0,sigma^2) cores, N(0,1) x)",
+        "config": {"workload": "c1+c2 decode suite: 1920->2880 (8,12,20)->(12,10,24), "
+                               "R8 T=1/8/32 and R16 T=1/32, fp16",
+                   "l2": "flushed (256 MiB write) before every timed call",
+                   "parallelism": f"replica x{world}" if world > 1 else "single GPU",
+                   "cases": per_case},
+        "e2e": {"value": round(statistics.mean(e2e), 3), "unit": "us/call",
+                "h2d_bytes_per_step": sum(cases[k]["h2d"] for k in keys),
+                "d2h_bytes_per_step": sum(cases[k]["d2h"] for k in keys)},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "kernel": f"ring_mma_kernel r{dk[0]} t{dk[1]}",
+                     "achieved": round(achieved, 2), "peak": tc_peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / tc_peak, 4), "traffic": traffic,
+                     "peak_kind": f"{peak_kind} bf16 dense (burst)"},
+        "clocks": clk,
+    }
+    if world == 1:
+        value_cpu, threads, cpu_cases = cpu_reference_leg(1.0)
+        line["cpu_baseline"] = {"value": round(value_cpu, 2), "unit": "us/call", "cores": threads,
+                                "kind": "port", "sample": "each of the 5 cases, repeated "
+                                "calls for ~1 s, median; numpy fp32 restatement of "
+                                "tr_forward_reference", "cases": cpu_cases}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,130 @@
+/*
+ * trring.h -- C ABI of the B200 (sm_100a) three-core tensor-ring linear operator.
+ *
+ *   y[t,(p,q,r)] = sum_{i,j,k,a,b,c} x[t,(i,j,k)] A[a,p,i,b] B[b,q,j,c] C[c,r,k,a]
+ *
+ * Cores use the reference's storage order [rank, output_mode, input_mode, rank]
+ * (factorized_inference/reference.py:17-21, 66-73); x is [tokens, i*j*k] row-major with the
+ * first input mode slowest, y is [tokens, p*q*r] with the first output mode slowest
+ * (reference.py:119,125).  The dense weight is never formed.
+ *
+ * Every entry point returns an int status (TR_OK == 0, negative on error); no C++ exception
+ * crosses this boundary.  The library never allocates device memory: packed cores and the
+ * workspace are buffers the caller owns, sized by tr_packed_bytes / tr_workspace_bytes.
+ * Device pointers are plain pointers on the plan's device; `stream` is a cudaStream_t
+ * (NULL = legacy default stream).
+ *
+ * Reference interfaces these replace (paths inside danila-permogorskii/kernel-task):
+ *   tr_plan_create + tr_pack_cores   <- PreparedTRKernel.__init__ and pack_cores
+ *                                       (src/factorized_inference/tr_kernel.py:190-228, 86-99)
+ *   tr_forward                       <- PreparedTRKernel.__call__ (tr_kernel.py:264-319) and
+ *                                       the extension entry points tr_ring_forward /
+ *                                       tr_ring_forward_v3 / tr_ring_forward_v3t
+ *                                       (src/factorized_inference/csrc/tr_ring.cu:448-463,
+ *                                       1108-1141, 1156-1192)
+ *   tr_workspace_bytes               <- the design-B workspace sizing in PreparedTRKernel.__call__
+ *                                       (tr_kernel.py:290-296, 314-317)
+ *   tr_plan_destroy                  <- releasing the PreparedTRKernel (Python GC in the reference)
+ */
+#ifndef TRRING_H
+#define TRRING_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The reference raises ValueError for shape errors (reference.py:27-31,85-96)
+ * and RuntimeError through TORCH_CHECK (tr_ring.cu:416-418,453-457); the torch binding maps
+ * TR_ERR_INVALID to ValueError and everything else to RuntimeError. */
+enum tr_status {
+  TR_OK = 0,
+  TR_ERR_INVALID = -1,     /* bad argument: shape, null pointer, unknown dtype, negative T   */
+  TR_ERR_UNSUPPORTED = -2, /* valid spec, but no kernel of this build handles it           */
+  TR_ERR_WORKSPACE = -3,   /* workspace pointer missing or smaller than tr_workspace_bytes */
+  TR_ERR_CUDA = -4,        /* a CUDA runtime call failed (message: tr_last_error)          */
+  TR_ERR_ALIGN = -5,       /* a pointer is not aligned as required (16 bytes)              */
+  TR_ERR_TIMEOUT = -6      /* a bounded device-side wait gave up (status word set)         */
+};
+
+/* Element types of cores, x and y (one type per plan). */
+enum tr_dtype { TR_F32 = 0, TR_F16 = 1, TR_BF16 = 2 };
+
+/* Shape of one operator.  Mirrors TRSpec (reference.py:15-50): one rank for all three ring
+ * links; core k has shape [rank, output_modes[k], input_modes[k], rank]. */
+typedef struct tr_spec {
+  int32_t input_modes[3];
+  int32_t output_modes[3];
+  int32_t rank;
+} tr_spec;
+
+/* Per-call kernel geometry override (tests and tuning).  Zero fields mean "planner's choice".
+ *   tokens_per_tile : tokens per CTA row tile
+ *   cluster         : CTAs per thread-block cluster that share one partial sum in DSMEM
+ *   clusters        : clusters per row tile (>1 adds the workspace slot reduction)
+ *   kernel          : 0 auto, 1 generic CUDA-core kernel, 2 mma.sync fused kernel,
+ *                     3 tcgen05 fused kernel                                                  */
+typedef struct tr_tiling {
+  int32_t tokens_per_tile;
+  int32_t cluster;
+  int32_t clusters;
+  int32_t kernel;
+} tr_tiling;
+
+typedef struct tr_plan tr_plan;
+
+/* Validate the spec, pick the contraction order (the cheapest of the six ring orders, no
+ * dense W), and lay out the packed cores.  Host only; no device memory is touched.
+ * `device` is the CUDA ordinal every later call must use.                                     */
+int tr_plan_create(const tr_spec* spec, int32_t dtype, int32_t device, tr_plan** out);
+void tr_plan_destroy(tr_plan* plan);
+
+/* Bytes of the packed-core buffer (16-byte aligned device memory, caller-owned). */
+int tr_packed_bytes(const tr_plan* plan, size_t* bytes);
+
+/* Pack the three caller cores (contiguous device tensors of the plan's dtype, shapes
+ * [R,o_k,i_k,R]) into `packed`.  Cores are read, never written.  Stream-ordered.             */
+int tr_pack_cores(const tr_plan* plan, const void* const cores[3], void* packed, void* stream);
+
+/* Workspace bytes tr_forward needs for `tokens` rows (0 when the chosen kernel needs none).
+ * A workspace must be zero-filled once before its first use (tr_workspace_clear); every
+ * forward leaves it ready for the next call.  One workspace serves one stream at a time.      */
+int tr_workspace_bytes(const tr_plan* plan, int64_t tokens, size_t* bytes);
+/* Workspace bytes for an explicit geometry (see tr_forward_tiled; NULL = planner's choice). */
+int tr_workspace_bytes_tiled(const tr_plan* plan, int64_t tokens, const struct tr_tiling* tiling,
+                             size_t* bytes);
+int tr_workspace_clear(void* workspace, size_t bytes, void* stream);
+
+/* y[tokens, d_out] = TR(x[tokens, d_in]).  x, y: contiguous row-major, plan dtype, 16-byte
+ * aligned.  tokens == 0 is a no-op.  Launches exactly one kernel on `stream`.                 */
+int tr_forward(const tr_plan* plan, const void* packed, const void* x, int64_t tokens, void* y,
+               void* workspace, size_t workspace_bytes, void* stream);
+
+/* Same as tr_forward with an explicit geometry (NULL = planner's choice). */
+int tr_forward_tiled(const tr_plan* plan, const void* packed, const void* x, int64_t tokens,
+                     void* y, void* workspace, size_t workspace_bytes, const tr_tiling* tiling,
+                     void* stream);
+
+/* The geometry tr_forward would use for `tokens` (after clamping to this device). */
+int tr_plan_tiling(const tr_plan* plan, int64_t tokens, tr_tiling* out);
+
+/* JSON description of the plan (order, canonical modes, packed layout, per-path FLOPs). */
+int tr_plan_describe(const tr_plan* plan, char* buf, size_t len);
+
+/* Algorithmic FLOPs per token of the chosen contraction order (2 * MACs). */
+int tr_plan_flops_per_token(const tr_plan* plan, double* flops);
+
+const char* tr_status_string(int status);
+/* Last error message of the calling thread (CUDA error text or argument diagnostics). */
+const char* tr_last_error(void);
+
+/* An empty kernel on `stream`: the launch floor the roofline is bounded by. */
+int tr_empty_launch(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TRRING_H */

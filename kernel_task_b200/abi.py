@@ -1,0 +1,134 @@
+"""ctypes view of libtrring.so (include/trring.h), for callers that reach the C ABI without
+the torch binding, and for the tests that exercise the ABI itself.  Pointers are plain
+integers (``tensor.data_ptr()``), streams are ``cudaStream_t`` handles as integers."""
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_char_p, c_double, c_int, c_int32, c_int64, c_size_t, c_void_p
+
+from ._native import LIBRARY
+
+TR_OK = 0
+TR_ERR_INVALID = -1
+TR_ERR_UNSUPPORTED = -2
+TR_ERR_WORKSPACE = -3
+TR_ERR_CUDA = -4
+TR_ERR_ALIGN = -5
+TR_ERR_TIMEOUT = -6
+TR_F32, TR_F16, TR_BF16 = 0, 1, 2
+KERNEL_AUTO, KERNEL_GENERIC, KERNEL_MMA, KERNEL_TC05 = 0, 1, 2, 3
+
+
+class TrSpec(ctypes.Structure):
+    _fields_ = [("input_modes", c_int32 * 3), ("output_modes", c_int32 * 3), ("rank", c_int32)]
+
+
+class TrTiling(ctypes.Structure):
+    _fields_ = [("tokens_per_tile", c_int32), ("cluster", c_int32), ("clusters", c_int32),
+                ("kernel", c_int32)]
+
+
+# name -> (restype, argtypes); every function declared in include/trring.h
+PROTOTYPES = {
+    "tr_plan_create": (c_int, [POINTER(TrSpec), c_int32, c_int32, POINTER(c_void_p)]),
+    "tr_plan_destroy": (None, [c_void_p]),
+    "tr_packed_bytes": (c_int, [c_void_p, POINTER(c_size_t)]),
+    "tr_pack_cores": (c_int, [c_void_p, POINTER(c_void_p), c_void_p, c_void_p]),
+    "tr_workspace_bytes": (c_int, [c_void_p, c_int64, POINTER(c_size_t)]),
+    "tr_workspace_bytes_tiled": (c_int, [c_void_p, c_int64, POINTER(TrTiling),
+                                         POINTER(c_size_t)]),
+    "tr_workspace_clear": (c_int, [c_void_p, c_size_t, c_void_p]),
+    "tr_forward": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_size_t,
+                           c_void_p]),
+    "tr_forward_tiled": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
+                                 c_size_t, POINTER(TrTiling), c_void_p]),
+    "tr_plan_tiling": (c_int, [c_void_p, c_int64, POINTER(TrTiling)]),
+    "tr_plan_describe": (c_int, [c_void_p, c_char_p, c_size_t]),
+    "tr_plan_flops_per_token": (c_int, [c_void_p, POINTER(c_double)]),
+    "tr_status_string": (c_char_p, [c_int]),
+    "tr_last_error": (c_char_p, []),
+    "tr_empty_launch": (c_int, [c_void_p]),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIBRARY.exists():
+            raise RuntimeError(f"{LIBRARY} is not built; run `python -m kernel_task_b200.build`")
+        handle = ctypes.CDLL(str(LIBRARY))
+        for name, (res, args) in PROTOTYPES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+class AbiError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        L = lib()
+        super().__init__(f"{what}: {L.tr_status_string(status).decode()} "
+                         f"({L.tr_last_error().decode()})")
+        self.status = status
+
+
+def check(status: int, what: str) -> None:
+    if status != TR_OK:
+        raise AbiError(status, what)
+
+
+class Plan:
+    """Owner of one tr_plan handle."""
+
+    def __init__(self, input_modes, output_modes, rank: int, dtype: int, device: int = 0):
+        spec = TrSpec((c_int32 * 3)(*input_modes), (c_int32 * 3)(*output_modes), rank)
+        handle = c_void_p()
+        check(lib().tr_plan_create(ctypes.byref(spec), dtype, device, ctypes.byref(handle)),
+              "tr_plan_create")
+        self.handle = handle
+
+    def __del__(self):
+        if getattr(self, "handle", None) and _lib is not None:
+            _lib.tr_plan_destroy(self.handle)
+            self.handle = None
+
+    def packed_bytes(self) -> int:
+        n = c_size_t()
+        check(lib().tr_packed_bytes(self.handle, ctypes.byref(n)), "tr_packed_bytes")
+        return n.value
+
+    def workspace_bytes(self, tokens: int, tiling: TrTiling | None = None) -> int:
+        n = c_size_t()
+        check(lib().tr_workspace_bytes_tiled(self.handle, tokens,
+                                             ctypes.byref(tiling) if tiling else None,
+                                             ctypes.byref(n)), "tr_workspace_bytes")
+        return n.value
+
+    def pack(self, core_ptrs, packed_ptr: int, stream: int = 0) -> None:
+        arr = (c_void_p * 3)(*core_ptrs)
+        check(lib().tr_pack_cores(self.handle, arr, c_void_p(packed_ptr), c_void_p(stream)),
+              "tr_pack_cores")
+
+    def forward(self, packed_ptr: int, x_ptr: int, tokens: int, y_ptr: int, ws_ptr: int = 0,
+                ws_bytes: int = 0, stream: int = 0, tiling: TrTiling | None = None) -> int:
+        return lib().tr_forward_tiled(self.handle, c_void_p(packed_ptr), c_void_p(x_ptr), tokens,
+                                      c_void_p(y_ptr), c_void_p(ws_ptr or None), ws_bytes,
+                                      ctypes.byref(tiling) if tiling else None, c_void_p(stream))
+
+    def tiling(self, tokens: int) -> TrTiling:
+        t = TrTiling()
+        check(lib().tr_plan_tiling(self.handle, tokens, ctypes.byref(t)), "tr_plan_tiling")
+        return t
+
+    def describe(self) -> str:
+        buf = ctypes.create_string_buffer(1024)
+        check(lib().tr_plan_describe(self.handle, buf, len(buf)), "tr_plan_describe")
+        return buf.value.decode()
+
+    def flops_per_token(self) -> float:
+        f = c_double()
+        check(lib().tr_plan_flops_per_token(self.handle, ctypes.byref(f)), "flops")
+        return f.value

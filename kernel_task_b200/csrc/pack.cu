@@ -1,0 +1,187 @@
+// Preparation: pack the caller's three cores [R, o, i, R] into kernel-native layouts.
+//
+// Replaces pack_cores (factorized_inference/tr_kernel.py:86-99).  Two layouts exist:
+//   * generic  -- the canonical cores G1, G2, G3 in natural [l][o][i][r] order, plan dtype;
+//   * mma      -- m16n8k16 B-operand fragments (one uint2 per lane per (k-step, n-tile)):
+//                   G1 frags  [s][ks1][nt1][lane]       K = i1,     N = (o1,u)   plan dtype
+//                   G2 frags  [ks2][nt2][lane]           K = (i2,u), N = (o2,v)   fp16
+//                   G3 frags  [piece][ks3][nt3][lane]    K = v,      N = o3       fp16
+//                 with piece = i3*R + s.  Ranks pad to RP (8/16/32) and modes to the tile
+//                 edges with zeros, which leaves every sum unchanged.
+// bf16 plans keep G1 in bf16 (S1 multiplies it with the bf16 x) and convert G2, G3 to fp16:
+// the S2/S3 intermediates are fp16 so that bf16 rounding of the ring intermediates does not
+// push the result past the 2e-3 relative Frobenius budget.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <type_traits>
+
+#include "device_util.cuh"
+#include "plan.h"
+
+namespace trr {
+
+// One canonical core read through the reference storage order.  `rev` swaps the two rank
+// axes (ring walked backwards).
+template <typename E>
+struct CoreView {
+  const E* p;
+  int O, I, R, rev;
+  __device__ __forceinline__ float at(int l, int o, int i, int r) const {
+    const int lo = rev ? r : l, ro = rev ? l : r;
+    return to_f32<E>(p[(((size_t)lo * O + o) * I + i) * R + ro]);
+  }
+};
+
+struct PackDims {
+  int I1, I2, I3, O1, O2, O3, R;
+  int RP, KS1, NT1, KS2, NT2, NT3, KS3, npieces;
+};
+
+template <typename E>
+__global__ void pack_generic_kernel(CoreView<E> c0, CoreView<E> c1, CoreView<E> c2, E* g1, E* g2,
+                                    E* g3, size_t n1, size_t n2, size_t n3) {
+  const size_t total = n1 + n2 + n3;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    const CoreView<E>* c;
+    E* out;
+    size_t e;
+    if (idx < n1) {
+      c = &c0; out = g1; e = idx;
+    } else if (idx < n1 + n2) {
+      c = &c1; out = g2; e = idx - n1;
+    } else {
+      c = &c2; out = g3; e = idx - n1 - n2;
+    }
+    const int r = (int)(e % c->R);
+    size_t q = e / c->R;
+    const int i = (int)(q % c->I);
+    q /= c->I;
+    const int o = (int)(q % c->O);
+    const int l = (int)(q / c->O);
+    out[e] = from_f32<E>(c->at(l, o, i, r));
+  }
+}
+
+// B fragment of m16n8k16 for lane (g, t4) = (lane/4, lane%4):
+//   x = {B[2t4][g], B[2t4+1][g]},  y = {B[2t4+8][g], B[2t4+9][g]}   (low half first)
+template <typename T, typename F>
+__device__ __forceinline__ uint2 make_frag(int kbase, int nbase, int lane, F&& b) {
+  const int g = lane >> 2, t4 = lane & 3;
+  const int n = nbase + g, k = kbase + 2 * t4;
+  uint2 out;
+  out.x = pack2<T>(b(k, n), b(k + 1, n));
+  out.y = pack2<T>(b(k + 8, n), b(k + 9, n));
+  return out;
+}
+
+template <typename E>
+__global__ void pack_mma_kernel(CoreView<E> c0, CoreView<E> c1, CoreView<E> c2, PackDims d,
+                                uint2* f1, uint2* f2, uint2* f3, size_t n1, size_t n2, size_t n3) {
+  const size_t total = n1 + n2 + n3;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    const int lane = (int)(idx & 31);
+    if (idx < n1) {
+      // G1 frags [s][ks1][nt1][lane]: B[k = i1][n = o1*RP + u] = G1[s, o1, i1, u]
+      size_t q = idx >> 5;
+      const int nt = (int)(q % d.NT1);
+      q /= d.NT1;
+      const int ks = (int)(q % d.KS1);
+      const int s = (int)(q / d.KS1);
+      f1[idx] = make_frag<E>(ks * 16, nt * 8, lane, [&](int k, int n) -> float {
+        const int o1 = n / d.RP, u = n % d.RP;
+        return (k < d.I1 && u < d.R) ? c0.at(s, o1, k, u) : 0.f;
+      });
+    } else if (idx < n1 + n2) {
+      // G2 frags [ks2][nt2][lane]: B[k = i2*RP + u][n = o2*RP + v] = G2[u, o2, i2, v]
+      const size_t e = idx - n1;
+      size_t q = e >> 5;
+      const int nt = (int)(q % d.NT2);
+      const int ks = (int)(q / d.NT2);
+      f2[e] = make_frag<__half>(ks * 16, nt * 8, lane, [&](int k, int n) -> float {
+        const int i2 = k / d.RP, u = k % d.RP;
+        const int o2 = n / d.RP, v = n % d.RP;
+        return (i2 < d.I2 && u < d.R && v < d.R) ? c1.at(u, o2, i2, v) : 0.f;
+      });
+    } else {
+      // G3 frags [piece][ks3][nt3][lane]: B[k = v][n = o3] = G3[v, o3, i3, s], piece = i3*R+s
+      const size_t e = idx - n1 - n2;
+      size_t q = e >> 5;
+      const int nt = (int)(q % d.NT3);
+      q /= d.NT3;
+      const int ks = (int)(q % d.KS3);
+      const int piece = (int)(q / d.KS3);
+      const int i3 = piece / d.R, s = piece % d.R;
+      f3[e] = make_frag<__half>(ks * 16, nt * 8, lane, [&](int k, int n) -> float {
+        return (k < d.R && n < d.O3) ? c2.at(k, n, i3, s) : 0.f;
+      });
+    }
+  }
+}
+
+template <typename E>
+static int pack_typed(const Plan& p, const void* const cores[3], void* packed, cudaStream_t st) {
+  const Canon& c = p.c;
+  CoreView<E> v[3];
+  for (int k = 0; k < 3; ++k) {
+    const int m = c.role[k];
+    v[k].p = static_cast<const E*>(cores[m]);
+    v[k].O = p.spec.output_modes[m];
+    v[k].I = p.spec.input_modes[m];
+    v[k].R = c.R;
+    v[k].rev = c.reversed;
+  }
+  char* base = static_cast<char*>(packed);
+  bool done = false;
+  if constexpr (!std::is_same<E, float>::value) {
+    if (p.mma_ok) {
+      done = true;
+      const MmaLayout& m = p.m;
+      PackDims d{c.I1, c.I2, c.I3, c.O1, c.O2, c.O3, c.R, m.RP, m.KS1, m.NT1, m.KS2, m.NT2, m.NT3,
+                 m.KS3, m.npieces};
+      const size_t n1 = m.bytes_g1 / 8, n2 = m.bytes_g2 / 8, n3 = m.bytes_g3 / 8;
+      const size_t total = n1 + n2 + n3;
+      const int blocks = (int)std::min<size_t>((total + 255) / 256, 4096);
+      pack_mma_kernel<E><<<blocks, 256, 0, st>>>(
+          v[0], v[1], v[2], d, reinterpret_cast<uint2*>(base + m.off_g1),
+          reinterpret_cast<uint2*>(base + m.off_g2), reinterpret_cast<uint2*>(base + m.off_g3),
+          n1, n2, n3);
+    }
+  }
+  if (!done) {
+    const GenericLayout& g = p.g;
+    const size_t total = g.elems_g1 + g.elems_g2 + g.elems_g3;
+    const int blocks = (int)std::min<size_t>((total + 255) / 256, 4096);
+    pack_generic_kernel<E><<<blocks, 256, 0, st>>>(
+        v[0], v[1], v[2], reinterpret_cast<E*>(base + g.off_g1),
+        reinterpret_cast<E*>(base + g.off_g2), reinterpret_cast<E*>(base + g.off_g3), g.elems_g1,
+        g.elems_g2, g.elems_g3);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("pack launch: %s", cudaGetErrorString(e));
+    return TR_ERR_CUDA;
+  }
+  return TR_OK;
+}
+
+int launch_pack(const Plan& p, const void* const cores[3], void* packed, void* stream) {
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess || cur != p.device) {
+    cudaGetLastError();
+    set_error("current device %d is not the plan's device %d", cur, p.device);
+    return TR_ERR_INVALID;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (p.dtype) {
+    case TR_F32: return pack_typed<float>(p, cores, packed, st);
+    case TR_F16: return pack_typed<__half>(p, cores, packed, st);
+    case TR_BF16: return pack_typed<__nv_bfloat16>(p, cores, packed, st);
+  }
+  set_error("unknown dtype");
+  return TR_ERR_INVALID;
+}
+
+}  // namespace trr

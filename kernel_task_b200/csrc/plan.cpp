@@ -1,0 +1,467 @@
+// Host planner of the tensor-ring operator: spec validation, contraction-order choice,
+// packed-core layout, per-call kernel geometry, and the C-ABI entry points that do not launch.
+//
+// Spec rules follow TRSpec.__post_init__ / _validate (reference.py:27-31, 85-96).  The order
+// choice replaces the reference's fixed x.A -> .B -> .C sequence (reference.py:122-124) by the
+// cheapest of the six ring orders; the arithmetic it evaluates is the same sum.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+
+#include "plan.h"
+
+namespace trr {
+
+static thread_local std::string g_last_error;
+
+void set_error(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+}
+
+static int ceil_div(int a, int b) { return (a + b - 1) / b; }
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Multiply-adds per token of order (X first, then Y, then Z) on the canonical chain
+//   S1: d_in*o_X*R^2   S2: i_Y*i_Z*o_X*o_Y*R^3   S3: d_out*i_Z*R^2
+static double order_macs(const tr_spec& s, int X, int Y, int Z) {
+  const double R = s.rank;
+  const double din = (double)s.input_modes[0] * s.input_modes[1] * s.input_modes[2];
+  const double dout = (double)s.output_modes[0] * s.output_modes[1] * s.output_modes[2];
+  return din * s.output_modes[X] * R * R +
+         (double)s.input_modes[Y] * s.input_modes[Z] * s.output_modes[X] * s.output_modes[Y] * R *
+             R * R +
+         dout * s.input_modes[Z] * R * R;
+}
+
+static void build_canon(const tr_spec& s, int X, int Y, Canon* c) {
+  const int Z = 3 - X - Y;
+  c->role[0] = X;
+  c->role[1] = Y;
+  c->role[2] = Z;
+  c->reversed = (Y == (X + 2) % 3) ? 1 : 0;  // Y precedes X on the ring A->B->C->A
+  c->I1 = s.input_modes[X];
+  c->I2 = s.input_modes[Y];
+  c->I3 = s.input_modes[Z];
+  c->O1 = s.output_modes[X];
+  c->O2 = s.output_modes[Y];
+  c->O3 = s.output_modes[Z];
+  c->R = s.rank;
+  c->d_in = s.input_modes[0] * s.input_modes[1] * s.input_modes[2];
+  c->d_out = s.output_modes[0] * s.output_modes[1] * s.output_modes[2];
+  const int64_t xs[3] = {(int64_t)s.input_modes[1] * s.input_modes[2], s.input_modes[2], 1};
+  const int64_t ys[3] = {(int64_t)s.output_modes[1] * s.output_modes[2], s.output_modes[2], 1};
+  c->sx1 = xs[X];
+  c->sx2 = xs[Y];
+  c->sx3 = xs[Z];
+  c->sy1 = ys[X];
+  c->sy2 = ys[Y];
+  c->sy3 = ys[Z];
+}
+
+static size_t elem_size(int dtype) { return dtype == TR_F32 ? 4 : 2; }
+
+static void build_mma_layout(Plan* p) {
+  const Canon& c = p->c;
+  MmaLayout& m = p->m;
+  m.RP = c.R <= 8 ? 8 : (c.R <= 16 ? 16 : 32);
+  m.K1P = ceil_div(c.I1, 16) * 16;
+  m.KS1 = m.K1P / 16;
+  m.NT1 = c.O1 * m.RP / 8;
+  m.K2P = ceil_div(c.I2 * m.RP, 16) * 16;
+  m.KS2 = m.K2P / 16;
+  m.NT2 = c.O2 * m.RP / 8;
+  m.O3P = ceil_div(c.O3, 8) * 8;
+  m.NT3 = m.O3P / 8;
+  m.KS3 = m.RP >= 16 ? m.RP / 16 : 1;
+  m.npieces = c.I3 * c.R;
+  const size_t frag = 32 * 8;  // one B fragment of a warp: 32 lanes x uint2
+  m.bytes_g1 = (size_t)c.R * m.KS1 * m.NT1 * frag;
+  m.bytes_g2 = (size_t)m.KS2 * m.NT2 * frag;
+  m.bytes_g3 = (size_t)m.npieces * m.KS3 * m.NT3 * frag;
+  m.off_g1 = 0;
+  m.off_g2 = align_up(m.off_g1 + m.bytes_g1, 256);
+  m.off_g3 = align_up(m.off_g2 + m.bytes_g2, 256);
+}
+
+static void build_generic_layout(Plan* p) {
+  const Canon& c = p->c;
+  GenericLayout& g = p->g;
+  const size_t es = elem_size(p->dtype);
+  g.elems_g1 = (size_t)c.R * c.O1 * c.I1 * c.R;
+  g.elems_g2 = (size_t)c.R * c.O2 * c.I2 * c.R;
+  g.elems_g3 = (size_t)c.R * c.O3 * c.I3 * c.R;
+  g.off_g1 = 0;
+  g.off_g2 = align_up(g.elems_g1 * es, 256);
+  g.off_g3 = align_up(g.off_g2 + g.elems_g2 * es, 256);
+}
+
+size_t mma_smem_bytes(const Plan& p, int TT, int NI3L, int MT2, int MT1) {
+  (void)TT;
+  const MmaLayout& m = p.m;
+  const size_t xs = align_up((size_t)NI3L * MT1 * 16 * (m.K1P + 8) * 2, 128);
+  const size_t t1 = (size_t)2 * MT2 * 16 * (m.K2P + 8) * 2;
+  const size_t ys = (size_t)MT2 * 16 * p.c.O2 * m.O3P * 4;
+  return align_up(std::max(xs + t1, ys), 128) + 128;  // + flag word area
+}
+
+// Largest count of distinct i3 values among the contiguous piece ranges of NJ CTAs.
+static int max_i3_span(int npieces, int R, int NJ) {
+  int best = 1;
+  for (int j = 0; j < NJ; ++j) {
+    const int pa = (int)((long long)j * npieces / NJ);
+    const int pb = (int)((long long)(j + 1) * npieces / NJ);
+    if (pb <= pa) continue;
+    const int span = (pb - 1) / R - pa / R + 1;
+    best = std::max(best, span);
+  }
+  return best;
+}
+
+int resolve_mma_geom(const Plan& p, int64_t T, const tr_tiling* f, MmaGeom* g) {
+  const Canon& c = p.c;
+  const MmaLayout& m = p.m;
+  if (!p.mma_ok) {
+    set_error("mma.sync kernel does not support this spec/dtype");
+    return TR_ERR_UNSUPPORTED;
+  }
+  // Compiled variants: (m16 row tiles per warp, max threads) = (1, 1024), (2, 512), (5, 384);
+  // one warp per o2, so O2 bounds the row tiles a CTA can hold.
+  const int mtw_max = c.O2 <= 12 ? 5 : (c.O2 <= 16 ? 2 : 1);
+  const int maxrows = mtw_max * 16;
+  int TT;
+  if (f && f->tokens_per_tile > 0) {
+    TT = f->tokens_per_tile;
+  } else if (T * c.O1 <= 16) {
+    TT = (int)T;
+  } else {
+    TT = std::max(1, maxrows / c.O1);
+  }
+  if (TT > T) TT = (int)T;
+  if (TT < 1) TT = 1;
+  const int MT2 = ceil_div(TT * c.O1, 16);
+  if (MT2 > mtw_max) {
+    set_error("tokens_per_tile=%d gives %d m16 tiles of S2 rows (max %d for O2=%d)", TT, MT2,
+              mtw_max, c.O2);
+    return TR_ERR_INVALID;
+  }
+  g->TT = TT;
+  g->MT2 = MT2;
+  g->MT1 = ceil_div(TT * c.I2, 16);
+  g->MTW = MT2 <= 1 ? 1 : (MT2 <= 2 ? 2 : 5);
+  g->ntiles = (int)((T + TT - 1) / TT);
+  g->NW = c.O2;
+  int CL, NC;
+  if (f && f->cluster > 0) {
+    CL = f->cluster;
+    NC = f->clusters > 0 ? f->clusters : 1;
+  } else {
+    int NJ = g->ntiles >= p.num_sms ? 1 : std::max(1, p.num_sms / g->ntiles);
+    NJ = std::min(NJ, m.npieces);
+    CL = std::min(8, NJ);
+    NC = std::max(1, NJ / CL);
+  }
+  if (CL < 1 || CL > 16 || NC < 1 || (long long)CL * NC > m.npieces) {
+    set_error("cluster=%d clusters=%d invalid for %d pieces", CL, NC, m.npieces);
+    return TR_ERR_INVALID;
+  }
+  g->CL = CL;
+  g->NC = NC;
+  g->NI3L = std::min(c.I3, max_i3_span(m.npieces, c.R, CL * NC));
+  g->smem = mma_smem_bytes(p, TT, g->NI3L, MT2, g->MT1);
+  if (g->smem > p.smem_optin) {
+    set_error("mma kernel needs %zu bytes of shared memory (device allows %zu)", g->smem,
+              p.smem_optin);
+    return TR_ERR_UNSUPPORTED;
+  }
+  g->ws_bytes = 0;
+  if (NC > 1) {
+    const size_t counters = align_up((size_t)g->ntiles * CL * sizeof(int), 256);
+    g->ws_bytes = counters + (size_t)g->ntiles * NC * TT * c.d_out * sizeof(float);
+  }
+  return TR_OK;
+}
+
+// Which kernel serves `T` tokens on this plan.
+static int pick_kind(const Plan& p, int64_t T, const tr_tiling* f) {
+  (void)T;
+  if (f && f->kernel != KIND_AUTO) return f->kernel;
+  if (p.mma_ok) return KIND_MMA;
+  return KIND_GENERIC;
+}
+
+}  // namespace trr
+
+using namespace trr;
+
+struct tr_plan : public trr::Plan {};
+
+extern "C" {
+
+const char* tr_status_string(int status) {
+  switch (status) {
+    case TR_OK: return "ok";
+    case TR_ERR_INVALID: return "invalid argument";
+    case TR_ERR_UNSUPPORTED: return "unsupported shape or dtype";
+    case TR_ERR_WORKSPACE: return "workspace missing or too small";
+    case TR_ERR_CUDA: return "CUDA error";
+    case TR_ERR_ALIGN: return "misaligned pointer";
+    case TR_ERR_TIMEOUT: return "device wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char* tr_last_error(void) { return g_last_error.c_str(); }
+
+int tr_plan_create(const tr_spec* spec, int32_t dtype, int32_t device, tr_plan** out) {
+  if (!spec || !out) {
+    set_error("null spec or output pointer");
+    return TR_ERR_INVALID;
+  }
+  *out = nullptr;
+  for (int k = 0; k < 3; ++k) {
+    if (spec->input_modes[k] <= 0 || spec->output_modes[k] <= 0) {
+      set_error("All modes and the rank must be positive");
+      return TR_ERR_INVALID;
+    }
+  }
+  if (spec->rank <= 0) {
+    set_error("All modes and the rank must be positive");
+    return TR_ERR_INVALID;
+  }
+  if (dtype != TR_F32 && dtype != TR_F16 && dtype != TR_BF16) {
+    set_error("unknown dtype %d", dtype);
+    return TR_ERR_INVALID;
+  }
+  const long long din = (long long)spec->input_modes[0] * spec->input_modes[1] * spec->input_modes[2];
+  const long long dout =
+      (long long)spec->output_modes[0] * spec->output_modes[1] * spec->output_modes[2];
+  if (din > (1LL << 30) || dout > (1LL << 30) || spec->rank > 4096) {
+    set_error("spec too large (d_in=%lld d_out=%lld rank=%d)", din, dout, spec->rank);
+    return TR_ERR_UNSUPPORTED;
+  }
+  tr_plan* p = new (std::nothrow) tr_plan();
+  if (!p) {
+    set_error("host allocation failed");
+    return TR_ERR_INVALID;
+  }
+  p->spec = *spec;
+  p->dtype = dtype;
+  p->device = device;
+  // cheapest order; ties keep the first in (X, Y) enumeration order
+  double best = -1.0;
+  int bx = 0, by = 1;
+  for (int X = 0; X < 3; ++X) {
+    for (int d = 1; d <= 2; ++d) {
+      const int Y = (X + d) % 3;
+      const int Z = 3 - X - Y;
+      const double macs = order_macs(*spec, X, Y, Z);
+      if (best < 0 || macs < best * (1.0 - 1e-12)) {
+        best = macs;
+        bx = X;
+        by = Y;
+      }
+    }
+  }
+  build_canon(*spec, bx, by, &p->c);
+  p->macs_per_token = best;
+  build_mma_layout(p);
+  build_generic_layout(p);
+  p->mma_ok = (dtype != TR_F32) && spec->rank <= 32 && p->c.O2 <= 32 && p->m.O3P <= 32 &&
+              p->c.O1 <= 80;
+  int nsm = 148;
+  int optin = 232448;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) == cudaSuccess) {
+    nsm = prop.multiProcessorCount;
+    optin = (int)prop.sharedMemPerBlockOptin;
+  } else {
+    cudaGetLastError();  // no device here: plan with B200 defaults
+  }
+  p->num_sms = nsm;
+  p->smem_optin = (size_t)optin;
+  if (p->mma_ok) {
+    p->packed_bytes = align_up(p->m.off_g3 + p->m.bytes_g3, 256);
+  } else {
+    p->packed_bytes = align_up(p->g.off_g3 + p->g.elems_g3 * elem_size(dtype), 256);
+  }
+  *out = p;
+  return TR_OK;
+}
+
+void tr_plan_destroy(tr_plan* plan) { delete plan; }
+
+int tr_packed_bytes(const tr_plan* plan, size_t* bytes) {
+  if (!plan || !bytes) {
+    set_error("null argument");
+    return TR_ERR_INVALID;
+  }
+  *bytes = plan->packed_bytes;
+  return TR_OK;
+}
+
+int tr_plan_flops_per_token(const tr_plan* plan, double* flops) {
+  if (!plan || !flops) {
+    set_error("null argument");
+    return TR_ERR_INVALID;
+  }
+  *flops = 2.0 * plan->macs_per_token;
+  return TR_OK;
+}
+
+static int geom_for(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling, int* kind,
+                    MmaGeom* g) {
+  if (!plan) {
+    set_error("null plan");
+    return TR_ERR_INVALID;
+  }
+  if (tokens < 0) {
+    set_error("negative token count");
+    return TR_ERR_INVALID;
+  }
+  *kind = pick_kind(*plan, tokens, tiling);
+  if (*kind == KIND_MMA) {
+    if (tokens == 0) {
+      memset(g, 0, sizeof(*g));
+      return TR_OK;
+    }
+    return resolve_mma_geom(*plan, tokens, tiling, g);
+  }
+  if (*kind == KIND_GENERIC) {
+    memset(g, 0, sizeof(*g));
+    return TR_OK;
+  }
+  set_error("kernel kind %d not available in this build", *kind);
+  return TR_ERR_UNSUPPORTED;
+}
+
+int tr_workspace_bytes_tiled(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling,
+                             size_t* bytes) {
+  if (!bytes) {
+    set_error("null argument");
+    return TR_ERR_INVALID;
+  }
+  int kind;
+  MmaGeom g;
+  const int st = geom_for(plan, tokens, tiling, &kind, &g);
+  if (st != TR_OK) return st;
+  *bytes = (kind == KIND_MMA) ? g.ws_bytes : 0;
+  return TR_OK;
+}
+
+int tr_workspace_bytes(const tr_plan* plan, int64_t tokens, size_t* bytes) {
+  return tr_workspace_bytes_tiled(plan, tokens, nullptr, bytes);
+}
+
+int tr_workspace_clear(void* workspace, size_t bytes, void* stream) {
+  if (bytes == 0) return TR_OK;
+  if (!workspace) {
+    set_error("null workspace");
+    return TR_ERR_INVALID;
+  }
+  const cudaError_t e = cudaMemsetAsync(workspace, 0, bytes, (cudaStream_t)stream);
+  if (e != cudaSuccess) {
+    set_error("cudaMemsetAsync: %s", cudaGetErrorString(e));
+    return TR_ERR_CUDA;
+  }
+  return TR_OK;
+}
+
+int tr_plan_tiling(const tr_plan* plan, int64_t tokens, tr_tiling* out) {
+  if (!out) {
+    set_error("null argument");
+    return TR_ERR_INVALID;
+  }
+  int kind;
+  MmaGeom g;
+  const int st = geom_for(plan, tokens, nullptr, &kind, &g);
+  if (st != TR_OK) return st;
+  out->kernel = kind;
+  out->tokens_per_tile = g.TT;
+  out->cluster = g.CL;
+  out->clusters = g.NC;
+  return TR_OK;
+}
+
+int tr_forward_tiled(const tr_plan* plan, const void* packed, const void* x, int64_t tokens,
+                     void* y, void* workspace, size_t workspace_bytes, const tr_tiling* tiling,
+                     void* stream) {
+  int kind;
+  MmaGeom g;
+  int st = geom_for(plan, tokens, tiling, &kind, &g);
+  if (st != TR_OK) return st;
+  if (tokens == 0) return TR_OK;
+  if (!packed || !x || !y) {
+    set_error("null packed, x or y pointer");
+    return TR_ERR_INVALID;
+  }
+  if (((uintptr_t)packed & 15) || ((uintptr_t)x & 15) || ((uintptr_t)y & 15)) {
+    set_error("packed, x and y must be 16-byte aligned");
+    return TR_ERR_ALIGN;
+  }
+  if (kind == KIND_GENERIC) return launch_generic(*plan, packed, x, tokens, y, stream);
+  if (g.ws_bytes > 0) {
+    if (!workspace || workspace_bytes < g.ws_bytes) {
+      set_error("workspace of %zu bytes needed, %zu given", g.ws_bytes,
+                workspace ? workspace_bytes : (size_t)0);
+      return TR_ERR_WORKSPACE;
+    }
+    if ((uintptr_t)workspace & 15) {
+      set_error("workspace must be 16-byte aligned");
+      return TR_ERR_ALIGN;
+    }
+  }
+  return launch_mma(*plan, g, packed, x, tokens, y, workspace, stream);
+}
+
+int tr_forward(const tr_plan* plan, const void* packed, const void* x, int64_t tokens, void* y,
+               void* workspace, size_t workspace_bytes, void* stream) {
+  return tr_forward_tiled(plan, packed, x, tokens, y, workspace, workspace_bytes, nullptr, stream);
+}
+
+int tr_pack_cores(const tr_plan* plan, const void* const cores[3], void* packed, void* stream) {
+  if (!plan || !cores || !cores[0] || !cores[1] || !cores[2] || !packed) {
+    set_error("null plan, core or packed pointer");
+    return TR_ERR_INVALID;
+  }
+  if ((uintptr_t)packed & 15) {
+    set_error("packed buffer must be 16-byte aligned");
+    return TR_ERR_ALIGN;
+  }
+  return launch_pack(*plan, cores, packed, stream);
+}
+
+int tr_plan_describe(const tr_plan* plan, char* buf, size_t len) {
+  if (!plan || !buf || len == 0) {
+    set_error("null argument");
+    return TR_ERR_INVALID;
+  }
+  const Canon& c = plan->c;
+  const MmaLayout& m = plan->m;
+  static const char* names = "ABC";
+  const int n = snprintf(
+      buf, len,
+      "{\"order\": \"%c%c%c\", \"reversed\": %d, \"canonical_in\": [%d, %d, %d], "
+      "\"canonical_out\": [%d, %d, %d], \"rank\": %d, \"macs_per_token\": %.0f, "
+      "\"mma\": %d, \"rank_padded\": %d, \"pieces\": %d, \"packed_bytes\": %zu, "
+      "\"dtype\": %d}",
+      names[c.role[0]], names[c.role[1]], names[c.role[2]], c.reversed, c.I1, c.I2, c.I3, c.O1,
+      c.O2, c.O3, c.R, plan->macs_per_token, plan->mma_ok, m.RP, m.npieces, plan->packed_bytes,
+      plan->dtype);
+  if (n < 0 || (size_t)n >= len) {
+    set_error("buffer too small");
+    return TR_ERR_INVALID;
+  }
+  return TR_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,97 @@
+// Internal plan structures shared by the host planner (plan.cpp) and the kernels (*.cu).
+//
+// Canonical ring.  Any of the six contraction orders of the three-core ring is rewritten as
+//     y[t,o1,o2,o3] = sum_{i1,i2,i3,s,u,v} x[t,i1,i2,i3] G1[s,o1,i1,u] G2[u,o2,i2,v] G3[v,o3,i3,s]
+// and contracted as  S1: x.G1 over i1  ->  S2: .G2 over (i2,u)  ->  S3: .G3 over (i3,s,v).
+// G1 is the reference core contracted first (role X), G2 the one sharing rank u with it (Y),
+// G3 the last (Z).  When Y precedes X on the reference ring (A->B->C->A) every core's two rank
+// axes are swapped while packing, so the kernels only ever see this one form.  The input and
+// output modes of the canonical form are strided views of x and y.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/trring.h"
+
+namespace trr {
+
+struct Canon {
+  int I1, I2, I3;          // canonical input modes  (x modes of cores X, Y, Z)
+  int O1, O2, O3;          // canonical output modes (y modes of cores X, Y, Z)
+  int R;                   // ring rank (all three links)
+  int d_in, d_out;
+  int64_t sx1, sx2, sx3;   // strides of i1,i2,i3 inside one x row
+  int64_t sy1, sy2, sy3;   // strides of o1,o2,o3 inside one y row
+  int role[3];             // reference core index playing X, Y, Z
+  int reversed;            // 1: ring walked C->B->A (rank axes swapped while packing)
+};
+
+// Fragment-ordered operand layout of the mma.sync fused kernel (ring_mma.cu).  Every packed
+// array stores, for each (k-step, n-tile) of an m16n8k16 B operand, the two 32-bit registers
+// of all 32 lanes back to back (256 bytes), so a warp loads a B fragment with one coalesced
+// 8-byte load per lane straight from L2 or shared memory.
+struct MmaLayout {
+  int RP;        // rank padded to the mma tile edge: 8, 16 or 32
+  int K1P, KS1;  // S1 contraction (i1) padded to 16, and its k16 steps
+  int NT1;       // S1 columns (o1,u): O1*RP/8 n8 tiles
+  int K2P, KS2;  // S2 contraction (i2,u): I2*RP padded to 16, k16 steps
+  int NT2;       // S2 columns (o2,v): O2*RP/8 n8 tiles
+  int O3P, NT3;  // S3 columns o3 padded to 8, n8 tiles
+  int KS3;       // S3 contraction v: RP/16 k16 steps (RP == 8 uses one m16n8k8 step)
+  int npieces;   // I3 * R pieces (i3, s) summed into y
+  size_t off_g1, off_g2, off_g3;  // byte offsets in the packed buffer
+  size_t bytes_g1, bytes_g2, bytes_g3;
+};
+
+// Canonical cores in natural [l][o][i][r] order (generic CUDA-core kernel, ring_generic.cu).
+struct GenericLayout {
+  size_t off_g1, off_g2, off_g3;
+  size_t elems_g1, elems_g2, elems_g3;
+};
+
+enum KernelKind { KIND_AUTO = 0, KIND_GENERIC = 1, KIND_MMA = 2, KIND_TC05 = 3 };
+
+struct Plan {
+  tr_spec spec;
+  int dtype;
+  int device;
+  Canon c;
+  double macs_per_token;  // chosen order, multiply-adds per token
+  int mma_ok;             // the mma.sync kernel handles this shape and dtype
+  MmaLayout m;
+  GenericLayout g;
+  size_t packed_bytes;
+  int num_sms;
+  size_t smem_optin;
+};
+
+// Geometry of one mma.sync launch (resolved from tr_tiling + the planner).
+struct MmaGeom {
+  int TT;        // tokens per row tile
+  int ntiles;    // ceil(T / TT)
+  int MT2;       // m16 tiles of S2/S3 rows (t,o1) per row tile
+  int MT1;       // m16 tiles of S1 rows (t,i2) per row tile
+  int MTW;       // compiled per-warp m16 tile capacity (>= MT2)
+  int CL;        // CTAs per cluster
+  int NC;        // clusters per row tile
+  int NW;        // warps per CTA (= O2)
+  int NI3L;      // largest number of distinct i3 values one CTA's pieces touch
+  size_t smem;   // dynamic shared memory bytes
+  size_t ws_bytes;
+};
+
+// Implemented in plan.cpp
+void set_error(const char* fmt, ...);
+int resolve_mma_geom(const Plan& p, int64_t T, const tr_tiling* force, MmaGeom* g);
+size_t mma_smem_bytes(const Plan& p, int TT, int NI3L, int MT2, int MT1);
+
+// Implemented in ring_mma.cu / ring_generic.cu / pack.cu
+int launch_pack(const Plan& p, const void* const cores[3], void* packed, void* stream);
+int launch_generic(const Plan& p, const void* packed, const void* x, int64_t T, void* y,
+                   void* stream);
+int launch_mma(const Plan& p, const MmaGeom& g, const void* packed, const void* x, int64_t T,
+               void* y, void* ws, void* stream);
+int query_max_active_clusters(const Plan& p, const MmaGeom& g, int* n);
+
+}  // namespace trr

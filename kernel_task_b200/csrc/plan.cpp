@@ -105,13 +105,27 @@ static void build_generic_layout(Plan* p) {
   g.off_g3 = align_up(g.off_g2 + g.elems_g2 * es, 256);
 }
 
-size_t mma_smem_bytes(const Plan& p, int TT, int NI3L, int MT2, int MT1) {
-  (void)TT;
+// Shared memory of one mma CTA:
+//   [x tile NI3L x M1P x (K1P+8)] [2 x T1 M2P x (K2P+8)] [G2 fragments]
+//   [G1+G3 fragments of each of the CTA's pieces] [raw x rows TT x d_in]
+// reused after the piece loop as [partial y TT x d_out fp32], + 128 B flag word.
+void mma_smem_layout(const Plan& p, MmaGeom* g) {
   const MmaLayout& m = p.m;
-  const size_t xs = align_up((size_t)NI3L * MT1 * 16 * (m.K1P + 8) * 2, 128);
-  const size_t t1 = (size_t)2 * MT2 * 16 * (m.K2P + 8) * 2;
-  const size_t ys = (size_t)MT2 * 16 * p.c.O2 * m.O3P * 4;
-  return align_up(std::max(xs + t1, ys), 128) + 128;  // + flag word area
+  const size_t es = 2;
+  const size_t xs = align_up((size_t)g->NI3L * g->MT1 * 16 * (m.K1P + 8) * es, 128);
+  const size_t t1 = align_up((size_t)g->MT2 * 16 * (m.K2P + 8) * 2, 128);
+  const size_t g2 = g->g2_smem ? align_up(m.bytes_g2, 128) : 0;
+  const size_t pf = g->pf_smem
+      ? align_up((size_t)g->PPC * (m.KS1 * m.NT1 + m.KS3 * m.NT3) * 256, 128) : 0;
+  const size_t xr = g->x_async ? align_up((size_t)g->TT * p.c.d_in * es, 128) : 0;
+  g->off_t1 = xs;
+  g->t1_stride = t1;
+  g->off_g2 = xs + 2 * t1;
+  g->off_pf = g->off_g2 + g2;
+  g->off_xr = g->off_pf + pf;
+  const size_t main = g->off_xr + xr;
+  const size_t ys = (size_t)g->TT * p.c.d_out * 4;
+  g->smem = align_up(std::max(main, ys), 128) + 128;  // + flag word area
 }
 
 // Largest count of distinct i3 values among the contiguous piece ranges of NJ CTAs.
@@ -177,7 +191,23 @@ int resolve_mma_geom(const Plan& p, int64_t T, const tr_tiling* f, MmaGeom* g) {
   g->CL = CL;
   g->NC = NC;
   g->NI3L = std::min(c.I3, max_i3_span(m.npieces, c.R, CL * NC));
-  g->smem = mma_smem_bytes(p, TT, g->NI3L, MT2, g->MT1);
+  g->PPC = ceil_div(m.npieces, CL * NC);
+  g->x_async = ((size_t)c.d_in * 2) % 16 == 0;
+  g->g2_smem = 1;
+  g->pf_smem = 1;
+  mma_smem_layout(p, g);
+  if (g->smem > p.smem_optin) {  // piece fragments too large to stage: read them from L2
+    g->pf_smem = 0;
+    mma_smem_layout(p, g);
+  }
+  if (g->smem > p.smem_optin) {  // G2 too large to stage: S2 reads it from L2
+    g->g2_smem = 0;
+    mma_smem_layout(p, g);
+  }
+  if (g->smem > p.smem_optin) {
+    g->x_async = 0;
+    mma_smem_layout(p, g);
+  }
   if (g->smem > p.smem_optin) {
     set_error("mma kernel needs %zu bytes of shared memory (device allows %zu)", g->smem,
               p.smem_optin);

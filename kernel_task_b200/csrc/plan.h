@@ -77,6 +77,11 @@ struct MmaGeom {
   int NC;        // clusters per row tile
   int NW;        // warps per CTA (= O2)
   int NI3L;      // largest number of distinct i3 values one CTA's pieces touch
+  int PPC;       // most pieces one CTA handles
+  int g2_smem;   // 1: G2 fragments staged in shared memory once per CTA
+  int pf_smem;   // 1: every piece's G1/G3 fragments staged in shared memory up front
+  int x_async;   // 1: x rows copied to shared memory asynchronously (rows 16-byte aligned)
+  size_t off_t1, t1_stride, off_g2, off_pf, off_xr;  // shared-memory carve-up (bytes)
   size_t smem;   // dynamic shared memory bytes
   size_t ws_bytes;
 };
@@ -84,7 +89,7 @@ struct MmaGeom {
 // Implemented in plan.cpp
 void set_error(const char* fmt, ...);
 int resolve_mma_geom(const Plan& p, int64_t T, const tr_tiling* force, MmaGeom* g);
-size_t mma_smem_bytes(const Plan& p, int TT, int NI3L, int MT2, int MT1);
+void mma_smem_layout(const Plan& p, MmaGeom* g);
 
 // Implemented in ring_mma.cu / ring_generic.cu / pack.cu
 int launch_pack(const Plan& p, const void* const cores[3], void* packed, void* stream);

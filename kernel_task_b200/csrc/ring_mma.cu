@@ -49,11 +49,59 @@ struct MmaParams {
   int role0, role1, role2;  // reference mode index of canonical mode 1, 2, 3
   int K1P, KS1, NT1, K2P, KS2, NT2, O3P, NT3, npieces;
   int TT, MT1, MT2, CL, NC, NI3L;
+  long long sy1, sy2, sy3;  // y strides of o1, o2, o3
+  // shared-memory carve-up (bytes; see mma_smem_layout in plan.cpp)
+  int off_t1, t1_stride, off_g2, off_pf, off_xr;
+  int g1p_bytes, g3p_bytes;  // fragments of one piece: G1 of its s, then G3 of the piece
+  int g2_smem, pf_smem, x_async, g2_bytes;
+  int vec4;                 // d_out % 4 == 0: reductions move float4
   int flag_off;
 };
 
 __device__ __forceinline__ int sel3(int k, int a, int b, int c) {
   return k == 0 ? a : (k == 1 ? b : c);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+}
+// All threads of the CTA copy `bytes` (multiple of 16) global -> shared, asynchronously.
+__device__ __forceinline__ void copy_async(unsigned char* dst, const void* src, int bytes,
+                                           int tid, int nthr) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(dst);
+  const char* g = static_cast<const char*>(src);
+  for (int i = tid * 16; i < bytes; i += nthr * 16) cp_async16(s + i, g + i);
+}
+
+// S2 for one warp: D2[mi][nv] += T1[rows of tile mi] . G2[:, o2 block], G2 fragments from
+// shared memory (SM) or global memory (!SM).
+template <int NV, int MTW, bool SM>
+__device__ __forceinline__ void s2_accumulate(float (&d2)[MTW][NV][4], const __half* t1, int T1STR,
+                                              const uint2* g2w, int KS2, int NT2, int MT2,
+                                              int lane) {
+  for (int ks2 = 0; ks2 < KS2; ++ks2) {
+    uint2 b[NV];
+#pragma unroll
+    for (int nv = 0; nv < NV; ++nv) {
+      const uint2* src = g2w + ((size_t)ks2 * NT2 + nv) * 32;
+      b[nv] = SM ? *src : __ldg(src);
+    }
+#pragma unroll
+    for (int mi = 0; mi < MTW; ++mi) {
+      if (mi < MT2) {
+        uint32_t a[4];
+        ldsm_x4(a, t1 + (size_t)(mi * 16 + (lane & 15)) * T1STR + ks2 * 16 + (lane >> 4) * 8);
+#pragma unroll
+        for (int nv = 0; nv < NV; ++nv) mma_16816(d2[mi][nv], a, b[nv].x, b[nv].y, __half());
+      }
+    }
+  }
 }
 
 template <typename E, int RP, int MTW, int MAXT>
@@ -72,32 +120,44 @@ __global__ void __launch_bounds__(MAXT, 1) ring_mma_kernel(const MmaParams p) {
   const int cl_id = jj / p.CL;
   const int pa = (int)((long long)jj * p.npieces / NJ);
   const int pb = (int)((long long)(jj + 1) * p.npieces / NJ);
+  const int np = pb - pa;
   const int t0 = tile * p.TT;
   const int TTv = min(p.TT, p.T - t0);
   const int i3a = pa / p.R;
-  const int i3b = pb > pa ? (pb - 1) / p.R + 1 : i3a;
+  const int i3b = np > 0 ? (pb - 1) / p.R + 1 : i3a;
 
   const int XSTR = p.K1P + 8;   // +16 B per row: ldmatrix rows fall in distinct banks
   const int M1P = p.MT1 * 16;
   const int T1STR = p.K2P + 8;
-  const int M2P = p.MT2 * 16;
-  const size_t xs_bytes = ((size_t)p.NI3L * M1P * XSTR * 2 + 127) / 128 * 128;
-  const size_t t1_bytes = (size_t)2 * M2P * T1STR * 2;
+  const int pf_stride = p.g1p_bytes + p.g3p_bytes;
   E* xs = reinterpret_cast<E*>(smem);
-  __half* t1s = reinterpret_cast<__half*>(smem + xs_bytes);
-  float* ys = reinterpret_cast<float*>(smem);  // reused after the piece loop
+  float* ys = reinterpret_cast<float*>(smem);  // [t][d_out] partial y, after the piece loop
   int* flag = reinterpret_cast<int*>(smem + p.flag_off);
+  const E* xg = static_cast<const E*>(p.x) + (size_t)t0 * p.d_in;
 
-  // ---- clear the x tile and both T1 buffers (padding rows/columns must read as zero)
-  {
+  // ---- prologue: one burst of async copies (G2, every piece's G1/G3 fragments, x rows)
+  if (p.g2_smem) copy_async(smem + p.off_g2, p.g2f, p.g2_bytes, tid, nthr);
+  if (p.pf_smem) {
+    for (int j = 0; j < np; ++j) {
+      const int pi = pa + j;
+      unsigned char* dst = smem + p.off_pf + j * pf_stride;
+      copy_async(dst, p.g1f + (size_t)(pi % p.R) * p.KS1 * p.NT1 * 32, p.g1p_bytes, tid, nthr);
+      copy_async(dst + p.g1p_bytes, p.g3f + (size_t)pi * KS3 * p.NT3 * 32, p.g3p_bytes, tid,
+                 nthr);
+    }
+  }
+  if (p.x_async) copy_async(smem + p.off_xr, xg, TTv * p.d_in * (int)sizeof(E), tid, nthr);
+  cp_async_commit();
+  {  // clear the x tile and both T1 buffers: padding rows/columns must read as zero
     uint4* z = reinterpret_cast<uint4*>(smem);
-    const int n16 = (int)((xs_bytes + t1_bytes) / 16);
+    const int n16 = (p.off_t1 + 2 * p.t1_stride) / 16;
     for (int e = tid; e < n16; e += nthr) z[e] = make_uint4(0u, 0u, 0u, 0u);
   }
   __syncthreads();
-  // ---- x tile: read rows in memory order (coalesced), scatter to xs[i3][(t,i2)][i1]
-  {
-    const E* x = static_cast<const E*>(p.x) + (size_t)t0 * p.d_in;
+  {  // x rows -> xs[i3][(t,i2)][i1]
+    const E* xsrc = p.x_async ? reinterpret_cast<const E*>(smem + p.off_xr) : xg;
+    if (p.x_async) cp_async_wait_all();
+    if (p.x_async) __syncthreads();
     const int n = TTv * p.d_in;
     for (int e = tid; e < n; e += nthr) {
       const int t = e / p.d_in, f = e - t * p.d_in;
@@ -107,9 +167,10 @@ __global__ void __launch_bounds__(MAXT, 1) ring_mma_kernel(const MmaParams p) {
       if (i3 < i3a || i3 >= i3b) continue;
       const int i1 = sel3(p.role0, m0, m1, m2);
       const int i2 = sel3(p.role1, m0, m1, m2);
-      xs[((size_t)(i3 - i3a) * M1P + t * p.I2 + i2) * XSTR + i1] = x[e];
+      xs[((size_t)(i3 - i3a) * M1P + t * p.I2 + i2) * XSTR + i1] = xsrc[e];
     }
   }
+  cp_async_wait_all();
   __syncthreads();
 
   const int o2 = warp;  // one o2 per warp (nwarps == O2)
@@ -121,51 +182,62 @@ __global__ void __launch_bounds__(MAXT, 1) ring_mma_kernel(const MmaParams p) {
 #pragma unroll
       for (int c = 0; c < 4; ++c) yacc[a][b][c] = 0.f;
 
-  const uint2* g2w = p.g2f + (size_t)o2 * NV * 32 + lane;
+  const uint2* g2s = reinterpret_cast<const uint2*>(smem + p.off_g2) + (size_t)o2 * NV * 32 + lane;
+  const uint2* g2g = p.g2f + (size_t)o2 * NV * 32 + lane;
   const int s1rows = TTv * p.I2;
   const int njobs1 = p.MT1 * p.NT1;
 
-  for (int pi = pa; pi < pb; ++pi) {
-    const int i3 = pi / p.R, s = pi - i3 * p.R;
-    const int buf = (pi - pa) & 1;
-    const E* xt = xs + (size_t)(i3 - i3a) * M1P * XSTR;
-    __half* t1 = t1s + (size_t)buf * M2P * T1STR;
-
-    // ---- S1: D1[(t,i2),(o1,u)] = x_i3 . G1_s, written as T1[(t,o1)][(i2,u)] (fp16)
-    const uint2* g1p = p.g1f + (size_t)s * p.KS1 * p.NT1 * 32 + lane;
-    for (int job = warp; job < njobs1; job += nwarps) {
-      const int mt1 = job / p.NT1, nt1 = job - mt1 * p.NT1;
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int ks = 0; ks < p.KS1; ++ks) {
-        uint32_t a[4];
-        ldsm_x4(a, xt + (size_t)(mt1 * 16 + (lane & 15)) * XSTR + ks * 16 + (lane >> 4) * 8);
-        const uint2 b = __ldg(g1p + (size_t)(ks * p.NT1 + nt1) * 32);
-        mma_16816(d, a, b.x, b.y, E());
-      }
-      const int col = nt1 * 8 + 2 * t4;
-      const int o1 = col / RP, u = col % RP;
+  // S1 of piece j+1 and S2/S3 of piece j share one iteration and one barrier (T1 is
+  // double-buffered), so each warp's instruction stream carries both.
+  for (int j = 0; j <= np; ++j) {
+    if (j < np) {
+      // ---- S1: D1[(t,i2),(o1,u)] = x_i3 . G1_s, written as T1[(t,o1)][(i2,u)] (fp16)
+      const int pi = pa + j;
+      const int i3 = pi / p.R;
+      const uint2* g1p = p.pf_smem
+          ? reinterpret_cast<const uint2*>(smem + p.off_pf + j * pf_stride) + lane
+          : p.g1f + (size_t)(pi % p.R) * p.KS1 * p.NT1 * 32 + lane;
+      const E* xt = xs + (size_t)(i3 - i3a) * M1P * XSTR;
+      __half* t1 = reinterpret_cast<__half*>(smem + p.off_t1 + (j & 1) * p.t1_stride);
+      for (int job = warp; job < njobs1; job += nwarps) {
+        const int mt1 = job / p.NT1, nt1 = job - mt1 * p.NT1;
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int ks = 0; ks < p.KS1; ++ks) {
+          uint32_t a[4];
+          ldsm_x4(a, xt + (size_t)(mt1 * 16 + (lane & 15)) * XSTR + ks * 16 + (lane >> 4) * 8);
+          const uint2* src = g1p + (size_t)(ks * p.NT1 + nt1) * 32;
+          const uint2 b = p.pf_smem ? *src : __ldg(src);
+          mma_16816(d, a, b.x, b.y, E());
+        }
+        const int col = nt1 * 8 + 2 * t4;
+        const int o1 = col / RP, u = col % RP;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int r = mt1 * 16 + g + 8 * h;
-        if (r < s1rows) {
-          const int t = r / p.I2, i2 = r - t * p.I2;
-          *reinterpret_cast<__half2*>(t1 + (size_t)(t * p.O1 + o1) * T1STR + i2 * RP + u) =
-              __floats2half2_rn(d[2 * h], d[2 * h + 1]);
+        for (int h = 0; h < 2; ++h) {
+          const int r = mt1 * 16 + g + 8 * h;
+          if (r < s1rows) {
+            const int t = r / p.I2, i2 = r - t * p.I2;
+            *reinterpret_cast<__half2*>(t1 + (size_t)(t * p.O1 + o1) * T1STR + i2 * RP + u) =
+                __floats2half2_rn(d[2 * h], d[2 * h + 1]);
+          }
         }
       }
     }
-    __syncthreads();  // T1[buf] complete; the other buffer is free for the next piece
-
-    if (o2 < p.O2) {
-      // G3 fragments of this piece (K = v, N = o3)
-      const uint2* g3p = p.g3f + (size_t)pi * KS3 * p.NT3 * 32 + lane;
+    if (j > 0 && o2 < p.O2) {
+      const int jp = j - 1;
+      const int pi = pa + jp;
+      const __half* t1 =
+          reinterpret_cast<const __half*>(smem + p.off_t1 + (jp & 1) * p.t1_stride);
+      const uint2* g3p = p.pf_smem
+          ? reinterpret_cast<const uint2*>(smem + p.off_pf + jp * pf_stride + p.g1p_bytes) + lane
+          : p.g3f + (size_t)pi * KS3 * p.NT3 * 32 + lane;
       uint2 b3[KS3][4];
 #pragma unroll
       for (int k = 0; k < KS3; ++k)
 #pragma unroll
-        for (int n = 0; n < 4; ++n)
-          b3[k][n] = n < p.NT3 ? __ldg(g3p + (size_t)(k * p.NT3 + n) * 32) : make_uint2(0u, 0u);
-
+        for (int n = 0; n < 4; ++n) {
+          const uint2* src = g3p + (size_t)(k * p.NT3 + n) * 32;
+          b3[k][n] = n < p.NT3 ? (p.pf_smem ? *src : __ldg(src)) : make_uint2(0u, 0u);
+        }
       // ---- S2: D2[(t,o1),(o2,v)] for this warp's o2, all row tiles
       float d2[MTW][NV][4];
 #pragma unroll
@@ -174,19 +246,10 @@ __global__ void __launch_bounds__(MAXT, 1) ring_mma_kernel(const MmaParams p) {
         for (int b = 0; b < NV; ++b)
 #pragma unroll
           for (int c = 0; c < 4; ++c) d2[a][b][c] = 0.f;
-      for (int ks2 = 0; ks2 < p.KS2; ++ks2) {
-        uint2 b[NV];
-#pragma unroll
-        for (int nv = 0; nv < NV; ++nv) b[nv] = __ldg(g2w + ((size_t)ks2 * p.NT2 + nv) * 32);
-#pragma unroll
-        for (int mi = 0; mi < MTW; ++mi) {
-          if (mi < p.MT2) {
-            uint32_t a[4];
-            ldsm_x4(a, t1 + (size_t)(mi * 16 + (lane & 15)) * T1STR + ks2 * 16 + (lane >> 4) * 8);
-#pragma unroll
-            for (int nv = 0; nv < NV; ++nv) mma_16816(d2[mi][nv], a, b[nv].x, b[nv].y, __half());
-          }
-        }
+      if (p.g2_smem) {
+        s2_accumulate<NV, MTW, true>(d2, t1, T1STR, g2s, p.KS2, p.NT2, p.MT2, lane);
+      } else {
+        s2_accumulate<NV, MTW, false>(d2, t1, T1STR, g2g, p.KS2, p.NT2, p.MT2, lane);
       }
       // ---- S3: Y[(t,o1),(o2,o3)] += D2 (as A, fp16) . G3_piece
 #pragma unroll
@@ -214,24 +277,26 @@ __global__ void __launch_bounds__(MAXT, 1) ring_mma_kernel(const MmaParams p) {
         }
       }
     }
+    __syncthreads();
   }
-  __syncthreads();  // every warp is done with xs / T1: reuse the space for the partial Y
 
-  // ---- partial Y -> ys[(t,o1)][o2*O3P + o3]
-  const int YSTR = p.O2 * p.O3P;
+  // ---- partial Y -> ys[t][y offset]: y memory order, so the reductions below move float4
   if (o2 < p.O2) {
 #pragma unroll
     for (int mi = 0; mi < MTW; ++mi) {
       if (mi < p.MT2) {
 #pragma unroll
-        for (int n = 0; n < 4; ++n) {
-          if (n < p.NT3) {
-            const int col = o2 * p.O3P + n * 8 + 2 * t4;
-            const int r0 = mi * 16 + g;
-            *reinterpret_cast<float2*>(ys + (size_t)r0 * YSTR + col) =
-                make_float2(yacc[mi][n][0], yacc[mi][n][1]);
-            *reinterpret_cast<float2*>(ys + (size_t)(r0 + 8) * YSTR + col) =
-                make_float2(yacc[mi][n][2], yacc[mi][n][3]);
+        for (int h = 0; h < 2; ++h) {
+          const int r = mi * 16 + g + 8 * h;
+          const int t = r / p.O1, o1 = r - t * p.O1;
+          if (t < TTv) {
+            float* row = ys + (size_t)t * p.d_out + o1 * p.sy1 + o2 * p.sy2;
+#pragma unroll
+            for (int n = 0; n < 4; ++n) {
+              const int o3 = n * 8 + 2 * t4;
+              if (o3 < p.O3) row[o3 * p.sy3] = yacc[mi][n][2 * h];
+              if (o3 + 1 < p.O3) row[(o3 + 1) * p.sy3] = yacc[mi][n][2 * h + 1];
+            }
           }
         }
       }
@@ -244,32 +309,52 @@ __global__ void __launch_bounds__(MAXT, 1) ring_mma_kernel(const MmaParams p) {
     __syncthreads();
   }
 
-  // ---- reduce this CTA's slice of the tile over the cluster, in y memory order
-  const int ntot = TTv * p.d_out;
-  const int ebeg = (int)((long long)crank * ntot / p.CL);
-  const int eend = (int)((long long)(crank + 1) * ntot / p.CL);
+  // ---- reduce this CTA's slice of the tile over the cluster (loads from every peer issued
+  // together, added in rank order), then write y (NC == 1) or this cluster's workspace slot
   E* y = static_cast<E*>(p.y) + (size_t)t0 * p.d_out;
-  float* slot =
-      p.NC > 1 ? p.slots + ((size_t)tile * p.NC + cl_id) * (size_t)p.TT * p.d_out : nullptr;
-  for (int e = ebeg + tid; e < eend; e += nthr) {
-    const int t = e / p.d_out, f = e - t * p.d_out;
-    const int m2 = f % p.ym2, q = f / p.ym2;
-    const int m1 = q % p.ym1, m0 = q / p.ym1;
-    const int oc1 = sel3(p.role0, m0, m1, m2);
-    const int oc2 = sel3(p.role1, m0, m1, m2);
-    const int oc3 = sel3(p.role2, m0, m1, m2);
-    const int idx = (t * p.O1 + oc1) * YSTR + oc2 * p.O3P + oc3;
-    float v;
-    if (p.CL > 1) {
-      v = 0.f;
-      for (int r = 0; r < p.CL; ++r) v += cluster.map_shared_rank(ys, r)[idx];
-    } else {
-      v = ys[idx];
+  const size_t sstride = (size_t)p.TT * p.d_out;
+  float* slot = p.NC > 1 ? p.slots + ((size_t)tile * p.NC + cl_id) * sstride : nullptr;
+  const int vw = p.vec4 ? 4 : 1;
+  const int nvec = TTv * p.d_out / vw;
+  const int vbeg = (int)((long long)crank * nvec / p.CL);
+  const int vend = (int)((long long)(crank + 1) * nvec / p.CL);
+  const float* peer[16];
+#pragma unroll
+  for (int r = 0; r < 16; ++r)
+    peer[r] = (p.CL > 1 && r < p.CL) ? cluster.map_shared_rank(ys, r) : ys;
+  if (p.vec4) {
+    for (int i = vbeg + tid; i < vend; i += nthr) {
+      float4 v[16];
+#pragma unroll
+      for (int r = 0; r < 16; ++r)
+        v[r] = r < p.CL ? reinterpret_cast<const float4*>(peer[r])[i] : make_float4(0, 0, 0, 0);
+      float4 s = v[0];
+#pragma unroll
+      for (int r = 1; r < 16; ++r) {
+        s.x += v[r].x; s.y += v[r].y; s.z += v[r].z; s.w += v[r].w;
+      }
+      if (p.NC == 1) {
+        uint2 o;
+        o.x = pack2<E>(s.x, s.y);
+        o.y = pack2<E>(s.z, s.w);
+        reinterpret_cast<uint2*>(y)[i] = o;
+      } else {
+        reinterpret_cast<float4*>(slot)[i] = s;
+      }
     }
-    if (p.NC == 1) {
-      y[e] = from_f32<E>(v);
-    } else {
-      slot[e] = v;
+  } else {
+    for (int i = vbeg + tid; i < vend; i += nthr) {
+      float v[16];
+#pragma unroll
+      for (int r = 0; r < 16; ++r) v[r] = r < p.CL ? peer[r][i] : 0.f;
+      float s = 0.f;
+#pragma unroll
+      for (int r = 0; r < 16; ++r) s += v[r];
+      if (p.NC == 1) {
+        y[i] = from_f32<E>(s);
+      } else {
+        slot[i] = s;
+      }
     }
   }
   if (p.CL > 1) cluster.sync();  // peers finished reading this CTA's shared memory
@@ -282,14 +367,42 @@ __global__ void __launch_bounds__(MAXT, 1) ring_mma_kernel(const MmaParams p) {
       *flag = (old == p.NC - 1);
     }
     __syncthreads();
-    if (*flag) {  // last cluster for this slice: add the NC slots and write y
+    if (*flag) {  // last cluster for this slice: add the NC slots in cluster order, write y
       __threadfence();
-      const float* s0 = p.slots + (size_t)tile * p.NC * (size_t)p.TT * p.d_out;
-      const size_t sstride = (size_t)p.TT * p.d_out;
-      for (int e = ebeg + tid; e < eend; e += nthr) {
-        float v = 0.f;
-        for (int c = 0; c < p.NC; ++c) v += __ldcg(s0 + c * sstride + e);
-        y[e] = from_f32<E>(v);
+      const float* s0 = p.slots + (size_t)tile * p.NC * sstride;
+      if (p.vec4) {
+        for (int i = vbeg + tid; i < vend; i += nthr) {
+          float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int c0 = 0; c0 < p.NC; c0 += 8) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              v[u] = c0 + u < p.NC
+                         ? __ldcg(reinterpret_cast<const float4*>(s0 + (c0 + u) * sstride) + i)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              s.x += v[u].x; s.y += v[u].y; s.z += v[u].z; s.w += v[u].w;
+            }
+          }
+          uint2 o;
+          o.x = pack2<E>(s.x, s.y);
+          o.y = pack2<E>(s.z, s.w);
+          reinterpret_cast<uint2*>(y)[i] = o;
+        }
+      } else {
+        for (int i = vbeg + tid; i < vend; i += nthr) {
+          float s = 0.f;
+          for (int c0 = 0; c0 < p.NC; c0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              v[u] = c0 + u < p.NC ? __ldcg(s0 + (c0 + u) * sstride + i) : 0.f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) s += v[u];
+          }
+          y[i] = from_f32<E>(s);
+        }
       }
       if (tid == 0) atomicExch(p.cnt + tile * p.CL + crank, 0);
     }
@@ -394,6 +507,19 @@ int launch_mma(const Plan& p, const MmaGeom& g, const void* packed, const void* 
   mp.O3P = m.O3P; mp.NT3 = m.NT3; mp.npieces = m.npieces;
   mp.TT = g.TT; mp.MT1 = g.MT1; mp.MT2 = g.MT2;
   mp.CL = g.CL; mp.NC = g.NC; mp.NI3L = g.NI3L;
+  mp.sy1 = c.sy1; mp.sy2 = c.sy2; mp.sy3 = c.sy3;
+  mp.off_t1 = (int)g.off_t1;
+  mp.t1_stride = (int)g.t1_stride;
+  mp.off_g2 = (int)g.off_g2;
+  mp.off_pf = (int)g.off_pf;
+  mp.off_xr = (int)g.off_xr;
+  mp.g1p_bytes = (int)(m.KS1 * m.NT1 * 256);
+  mp.g3p_bytes = (int)(m.KS3 * m.NT3 * 256);
+  mp.g2_smem = g.g2_smem;
+  mp.pf_smem = g.pf_smem;
+  mp.x_async = g.x_async;
+  mp.g2_bytes = (int)m.bytes_g2;
+  mp.vec4 = (c.d_out % 4 == 0) ? 1 : 0;
   mp.flag_off = (int)(g.smem - 128);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;

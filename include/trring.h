@@ -107,6 +107,23 @@ int tr_forward_tiled(const tr_plan* plan, const void* packed, const void* x, int
                      void* y, void* workspace, size_t workspace_bytes, const tr_tiling* tiling,
                      void* stream);
 
+/* tr_forward without a caller workspace, for callers that cannot allocate device memory:
+ * for example a plugin or foreign-language host that has no CUDA allocator of its own, or a
+ * serving loop that must not call cudaMalloc (it can synchronise the device) once running.
+ * It has no counterpart in the reference, whose callers always own a torch allocator.
+ *
+ * The scratch it needs lives in a fixed 8 MiB array inside this library (TR_NOALLOC_SCRATCH_
+ * BYTES), which every GPU that loads the library holds until the process exits.  A call whose
+ * token count needs more returns TR_ERR_WORKSPACE; use tr_forward with a workspace instead.
+ * The call allocates nothing: no cudaMalloc, cudaFree or allocating library routine.  Its first
+ * call on a device looks up the array's device address on that device; make that first call
+ * before any stream capture.  All calls share the one array and it keeps the last call's
+ * contents, so calls whose kernels overlap on the GPU (two streams, two threads) race and give
+ * wrong results; issue them in one stream order.  fp16/bf16 plans only.                       */
+#define TR_NOALLOC_SCRATCH_BYTES (8u << 20)
+int tr_forward_noalloc(const tr_plan* plan, const void* packed, const void* x, int64_t tokens,
+                       void* y, void* stream);
+
 /* The geometry tr_forward would use for `tokens` (after clamping to this device). */
 int tr_plan_tiling(const tr_plan* plan, int64_t tokens, tr_tiling* out);
 

@@ -42,6 +42,7 @@ PROTOTYPES = {
                            c_void_p]),
     "tr_forward_tiled": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
                                  c_size_t, POINTER(TrTiling), c_void_p]),
+    "tr_forward_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
     "tr_plan_tiling": (c_int, [c_void_p, c_int64, POINTER(TrTiling)]),
     "tr_plan_describe": (c_int, [c_void_p, c_char_p, c_size_t]),
     "tr_plan_flops_per_token": (c_int, [c_void_p, POINTER(c_double)]),
@@ -117,6 +118,12 @@ class Plan:
         return lib().tr_forward_tiled(self.handle, c_void_p(packed_ptr), c_void_p(x_ptr), tokens,
                                       c_void_p(y_ptr), c_void_p(ws_ptr or None), ws_bytes,
                                       ctypes.byref(tiling) if tiling else None, c_void_p(stream))
+
+    def forward_noalloc(self, packed_ptr: int, x_ptr: int, tokens: int, y_ptr: int,
+                        stream: int = 0) -> int:
+        """tr_forward with the library's built-in scratch (no caller workspace)."""
+        return lib().tr_forward_noalloc(self.handle, c_void_p(packed_ptr), c_void_p(x_ptr),
+                                        tokens, c_void_p(y_ptr), c_void_p(stream))
 
     def tiling(self, tokens: int) -> TrTiling:
         t = TrTiling()

@@ -458,6 +458,32 @@ int tr_forward(const tr_plan* plan, const void* packed, const void* x, int64_t t
   return tr_forward_tiled(plan, packed, x, tokens, y, workspace, workspace_bytes, nullptr, stream);
 }
 
+int tr_forward_noalloc(const tr_plan* plan, const void* packed, const void* x, int64_t tokens,
+                       void* y, void* stream) {
+  if (!plan) {
+    set_error("null plan");
+    return TR_ERR_INVALID;
+  }
+  if (tokens < 0) {
+    set_error("negative token count");
+    return TR_ERR_INVALID;
+  }
+  if (tokens == 0) return TR_OK;
+  if (!plan->mma_ok) {
+    set_error("the no-alloc entry point serves fp16/bf16 plans of the mma kernel");
+    return TR_ERR_UNSUPPORTED;
+  }
+  if (!packed || !x || !y) {
+    set_error("null packed, x or y pointer");
+    return TR_ERR_INVALID;
+  }
+  if (((uintptr_t)packed & 15) || ((uintptr_t)x & 15) || ((uintptr_t)y & 15)) {
+    set_error("packed, x and y must be 16-byte aligned");
+    return TR_ERR_ALIGN;
+  }
+  return forward_noalloc(*plan, packed, x, tokens, y, stream);
+}
+
 int tr_pack_cores(const tr_plan* plan, const void* const cores[3], void* packed, void* stream) {
   if (!plan || !cores || !cores[0] || !cores[1] || !cores[2] || !packed) {
     set_error("null plan, core or packed pointer");

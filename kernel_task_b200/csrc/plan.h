@@ -98,5 +98,7 @@ int launch_generic(const Plan& p, const void* packed, const void* x, int64_t T, 
 int launch_mma(const Plan& p, const MmaGeom& g, const void* packed, const void* x, int64_t T,
                void* y, void* ws, void* stream);
 int query_max_active_clusters(const Plan& p, const MmaGeom& g, int* n);
+int forward_noalloc(const Plan& p, const void* packed, const void* x, int64_t T, void* y,
+                    void* stream);
 
 }  // namespace trr

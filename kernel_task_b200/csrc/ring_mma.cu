@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "device_util.cuh"
 #include "plan.h"
@@ -542,6 +543,72 @@ int query_max_active_clusters(const Plan& p, const MmaGeom& g, int* n) {
   (void)g;
   *n = -1;
   return TR_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Scratch for tr_forward_noalloc: a fixed array in the module image, so that entry point never
+// asks the allocator for memory.  Every GPU that loads this library holds kNoAllocScratchBytes
+// for it until the process exits.
+constexpr size_t kNoAllocScratchBytes = TR_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// The array's device address on `device` (the current device).  Host code cannot use the
+// symbol itself: on the host it names a stand-in object, not device memory.  Looked up once
+// per device, on that device's first no-alloc call.
+static int noalloc_scratch(int device, void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  if (device < 0 || device >= 64) {
+    set_error("device ordinal %d out of range", device);
+    return TR_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[device]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr) {
+      cudaGetLastError();
+      set_error("cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+      return TR_ERR_CUDA;
+    }
+    addr[device] = ptr;
+  }
+  *out = addr[device];
+  return TR_OK;
+}
+
+int forward_noalloc(const Plan& p, const void* packed, const void* x, int64_t T, void* y,
+                    void* stream) {
+  if (T == 0) return TR_OK;
+  MmaGeom g;
+  int st = resolve_mma_geom(p, T, nullptr, &g);
+  if (st != TR_OK) return st;
+  if (g.ws_bytes > kNoAllocScratchBytes) {
+    set_error("%lld tokens need %zu bytes of scratch; the no-alloc entry point has %zu "
+              "(use tr_forward with a caller workspace)",
+              (long long)T, g.ws_bytes, kNoAllocScratchBytes);
+    return TR_ERR_WORKSPACE;
+  }
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess || cur != p.device) {
+    cudaGetLastError();
+    set_error("current device %d is not the plan's device %d", cur, p.device);
+    return TR_ERR_INVALID;
+  }
+  void* scratch = nullptr;
+  st = noalloc_scratch(p.device, &scratch);
+  if (st != TR_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (g.ws_bytes > 0) {
+    // the arrival counters must read zero when the kernel starts
+    const size_t counters = ((size_t)g.ntiles * g.CL * sizeof(int) + 255) / 256 * 256;
+    const cudaError_t e = cudaMemsetAsync(scratch, 0, counters, s);
+    if (e != cudaSuccess) {
+      set_error("cudaMemsetAsync(scratch counters): %s", cudaGetErrorString(e));
+      return TR_ERR_CUDA;
+    }
+  }
+  return launch_mma(p, g, packed, x, T, y, scratch, stream);
 }
 
 }  // namespace trr

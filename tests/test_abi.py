@@ -178,3 +178,23 @@ def test_ctypes_plan_lifecycle():
     assert lib.tr_packed_bytes(h, ctypes.byref(n)) == abi.TR_OK and n.value > 0
     lib.tr_plan_destroy(h)
     assert lib.tr_plan_create(None, 0, 0, ctypes.byref(h)) == abi.TR_ERR_INVALID
+
+
+def test_noalloc_entry_point_arguments_need_no_device():
+    """tr_forward_noalloc: argument errors are reported before any CUDA call, fp32 plans are
+    not served, and the documented scratch size matches the header."""
+    text = HEADER.read_text()
+    assert re.search(r"#define TR_NOALLOC_SCRATCH_BYTES \(8u << 20\)", text)
+    s = kspec.SPEC_C1
+    p16 = abi.Plan(s.input_modes, s.output_modes, s.rank, abi.TR_F16)
+    p32 = abi.Plan(s.input_modes, s.output_modes, s.rank, abi.TR_F32)
+    assert p16.forward_noalloc(0, 0, 0, 0) == abi.TR_OK           # T == 0 is a no-op
+    assert p16.forward_noalloc(16, 16, -1, 16) == abi.TR_ERR_INVALID
+    assert p16.forward_noalloc(0, 16, 1, 16) == abi.TR_ERR_INVALID
+    assert p16.forward_noalloc(16, 24, 1, 16) == abi.TR_ERR_ALIGN
+    assert p32.forward_noalloc(16, 16, 1, 16) == abi.TR_ERR_UNSUPPORTED
+    # the planner's geometry fits the built-in scratch for every benchmark shape and size
+    for sp in (kspec.SPEC_C1, kspec.SPEC_C2, *kspec.SPEC_C4.values()):
+        p = abi.Plan(sp.input_modes, sp.output_modes, sp.rank, abi.TR_F16)
+        for T in (1, 2, 3, 5, 8, 16, 32, 64, 128, 1000):
+            assert p.workspace_bytes(T) <= (8 << 20)

@@ -64,8 +64,9 @@ typedef struct tr_spec {
  *   tokens_per_tile : tokens per CTA row tile
  *   cluster         : CTAs per thread-block cluster that share one partial sum in DSMEM
  *   clusters        : clusters per row tile (>1 adds the workspace slot reduction)
- *   kernel          : 0 auto, 1 generic CUDA-core kernel, 2 mma.sync fused kernel,
- *                     3 tcgen05 fused kernel                                                  */
+ *   kernel          : 0 auto, 1 generic CUDA-core kernel, 2 mma.sync fused tile kernel,
+ *                     3 tcgen05 fused kernel, 4 mma.sync decode kernel (T*o1 <= 16; here
+ *                     `cluster` splits the pieces and `clusters` the output modes)          */
 typedef struct tr_tiling {
   int32_t tokens_per_tile;
   int32_t cluster;

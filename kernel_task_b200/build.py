@@ -19,7 +19,7 @@ INCLUDE = ROOT / "include"
 LIB = PKG / "libtrring.so"
 EXT = PKG / "_trring_torch.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CUDA_SOURCES = ["plan.cpp", "pack.cu", "ring_generic.cu", "ring_mma.cu"]
+CUDA_SOURCES = ["plan.cpp", "pack.cu", "ring_generic.cu", "ring_mma.cu", "ring_decode.cu"]
 
 
 def _nvcc() -> str:

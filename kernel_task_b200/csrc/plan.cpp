@@ -221,11 +221,66 @@ int resolve_mma_geom(const Plan& p, int64_t T, const tr_tiling* f, MmaGeom* g) {
   return TR_OK;
 }
 
+// Decode geometry: S2 rows (t, o1) fit one m16 tile.  Clusters of CL CTAs split the pieces;
+// NOC clusters split the output modes o2 into chunks of O2C (<= 4, the kernel's capacity).
+int resolve_decode_geom(const Plan& p, int64_t T, const tr_tiling* f, DecodeGeom* g) {
+  const Canon& c = p.c;
+  const MmaLayout& m = p.m;
+  const int variant = decode_variant(p);
+  if (!p.mma_ok || variant < 0 || T < 1 || T * c.O1 > 16) {
+    set_error("decode kernel needs T*O1 <= 16, rank <= 16 and an fp16/bf16 plan");
+    return TR_ERR_UNSUPPORTED;
+  }
+  g->MT1 = ceil_div((int)T * c.I2, 16);
+  if (g->MT1 > 2) {
+    set_error("decode kernel: %lld tokens x %d S1 rows exceed two m16 tiles", (long long)T, c.I2);
+    return TR_ERR_UNSUPPORTED;
+  }
+  const int CL = (f && f->cluster > 0) ? f->cluster : std::min(16, m.npieces);
+  if (CL < 1 || CL > 16 || CL > m.npieces) {
+    set_error("cluster=%d invalid for %d pieces", CL, m.npieces);
+    return TR_ERR_INVALID;
+  }
+  int NOC = (f && f->clusters > 0) ? f->clusters
+                                   : std::max(1, std::min(c.O2, p.num_sms / CL));
+  int O2C = ceil_div(c.O2, NOC);
+  if (O2C > 4) O2C = 4;
+  NOC = ceil_div(c.O2, O2C);
+  const int maxw = decode_max_threads(variant) / 32;
+  const int ppc = ceil_div(m.npieces, CL);
+  g->CL = CL;
+  g->NW = std::min(ppc, maxw);
+  const size_t t1 = (size_t)16 * (m.K2P + 8) * 2;
+  const size_t yw = (size_t)16 * 4 * m.O3P * 4;
+  g->warp_bytes = align_up(std::max(t1, yw), 16);
+  for (;;) {
+    g->O2C = O2C;
+    g->NOC = NOC;
+    g->off_warps = align_up((size_t)m.KS2 * O2C * (m.RP / 8) * 256, 128);
+    g->smem = g->off_warps + (size_t)g->NW * g->warp_bytes;
+    if (g->smem <= p.smem_optin) break;
+    if (g->NW > 4) {
+      g->NW = std::max(4, g->NW / 2);
+    } else if (O2C > 1) {
+      O2C -= 1;
+      NOC = ceil_div(c.O2, O2C);
+    } else {
+      set_error("decode kernel needs %zu bytes of shared memory", g->smem);
+      return TR_ERR_UNSUPPORTED;
+    }
+  }
+  return TR_OK;
+}
+
 // Which kernel serves `T` tokens on this plan.
 static int pick_kind(const Plan& p, int64_t T, const tr_tiling* f) {
-  (void)T;
   if (f && f->kernel != KIND_AUTO) return f->kernel;
-  if (p.mma_ok) return KIND_MMA;
+  if (p.mma_ok) {
+    DecodeGeom d;
+    if (T >= 1 && T * p.c.O1 <= 16 && resolve_decode_geom(p, T, nullptr, &d) == TR_OK)
+      return KIND_DECODE;
+    return KIND_MMA;
+  }
   return KIND_GENERIC;
 }
 
@@ -349,7 +404,7 @@ int tr_plan_flops_per_token(const tr_plan* plan, double* flops) {
 }
 
 static int geom_for(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling, int* kind,
-                    MmaGeom* g) {
+                    MmaGeom* g, DecodeGeom* dg) {
   if (!plan) {
     set_error("null plan");
     return TR_ERR_INVALID;
@@ -370,6 +425,11 @@ static int geom_for(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling
     memset(g, 0, sizeof(*g));
     return TR_OK;
   }
+  if (*kind == KIND_DECODE) {
+    memset(g, 0, sizeof(*g));
+    if (tokens == 0) return TR_OK;
+    return resolve_decode_geom(*plan, tokens, tiling, dg);
+  }
   set_error("kernel kind %d not available in this build", *kind);
   return TR_ERR_UNSUPPORTED;
 }
@@ -382,7 +442,8 @@ int tr_workspace_bytes_tiled(const tr_plan* plan, int64_t tokens, const tr_tilin
   }
   int kind;
   MmaGeom g;
-  const int st = geom_for(plan, tokens, tiling, &kind, &g);
+  DecodeGeom dg;
+  const int st = geom_for(plan, tokens, tiling, &kind, &g, &dg);
   if (st != TR_OK) return st;
   *bytes = (kind == KIND_MMA) ? g.ws_bytes : 0;
   return TR_OK;
@@ -413,9 +474,16 @@ int tr_plan_tiling(const tr_plan* plan, int64_t tokens, tr_tiling* out) {
   }
   int kind;
   MmaGeom g;
-  const int st = geom_for(plan, tokens, nullptr, &kind, &g);
+  DecodeGeom dg;
+  const int st = geom_for(plan, tokens, nullptr, &kind, &g, &dg);
   if (st != TR_OK) return st;
   out->kernel = kind;
+  if (kind == KIND_DECODE) {
+    out->tokens_per_tile = (int32_t)tokens;
+    out->cluster = dg.CL;
+    out->clusters = dg.NOC;
+    return TR_OK;
+  }
   out->tokens_per_tile = g.TT;
   out->cluster = g.CL;
   out->clusters = g.NC;
@@ -427,7 +495,8 @@ int tr_forward_tiled(const tr_plan* plan, const void* packed, const void* x, int
                      void* stream) {
   int kind;
   MmaGeom g;
-  int st = geom_for(plan, tokens, tiling, &kind, &g);
+  DecodeGeom dg;
+  int st = geom_for(plan, tokens, tiling, &kind, &g, &dg);
   if (st != TR_OK) return st;
   if (tokens == 0) return TR_OK;
   if (!packed || !x || !y) {
@@ -439,6 +508,7 @@ int tr_forward_tiled(const tr_plan* plan, const void* packed, const void* x, int
     return TR_ERR_ALIGN;
   }
   if (kind == KIND_GENERIC) return launch_generic(*plan, packed, x, tokens, y, stream);
+  if (kind == KIND_DECODE) return launch_decode(*plan, dg, packed, x, tokens, y, stream);
   if (g.ws_bytes > 0) {
     if (!workspace || workspace_bytes < g.ws_bytes) {
       set_error("workspace of %zu bytes needed, %zu given", g.ws_bytes,

@@ -50,7 +50,7 @@ struct GenericLayout {
   size_t elems_g1, elems_g2, elems_g3;
 };
 
-enum KernelKind { KIND_AUTO = 0, KIND_GENERIC = 1, KIND_MMA = 2, KIND_TC05 = 3 };
+enum KernelKind { KIND_AUTO = 0, KIND_GENERIC = 1, KIND_MMA = 2, KIND_TC05 = 3, KIND_DECODE = 4 };
 
 struct Plan {
   tr_spec spec;
@@ -86,6 +86,18 @@ struct MmaGeom {
   size_t ws_bytes;
 };
 
+// Geometry of one decode launch (ring_decode.cu): NOC clusters of CL CTAs of NW warps.
+struct DecodeGeom {
+  int CL;        // CTAs per cluster; they split the I3*R pieces
+  int NOC;       // clusters = chunks of O2C output modes o2
+  int O2C;       // o2 modes per cluster
+  int NW;        // warps per CTA (one piece per warp at a time)
+  int MT1;       // m16 tiles of S1 rows (t, i2): 1 or 2
+  size_t warp_bytes;  // per-warp shared area (T1 tile, then the warp's partial Y)
+  size_t off_warps;   // after the staged G2 chunk
+  size_t smem;
+};
+
 // Implemented in plan.cpp
 void set_error(const char* fmt, ...);
 int resolve_mma_geom(const Plan& p, int64_t T, const tr_tiling* force, MmaGeom* g);
@@ -100,5 +112,10 @@ int launch_mma(const Plan& p, const MmaGeom& g, const void* packed, const void* 
 int query_max_active_clusters(const Plan& p, const MmaGeom& g, int* n);
 int forward_noalloc(const Plan& p, const void* packed, const void* x, int64_t T, void* y,
                     void* stream);
+int resolve_decode_geom(const Plan& p, int64_t T, const tr_tiling* force, DecodeGeom* g);
+int decode_variant(const Plan& p);
+int decode_max_threads(int variant);
+int launch_decode(const Plan& p, const DecodeGeom& g, const void* packed, const void* x,
+                  int64_t T, void* y, void* stream);
 
 }  // namespace trr

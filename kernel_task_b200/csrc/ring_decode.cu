@@ -1,0 +1,374 @@
+// Decode kernel: the fused tensor-ring operator for token counts whose S2 rows (t, o1) fit one
+// m16 tile (T * O1 <= 16; T = 1 for every benchmark shape).  One launch, no workspace, no
+// global atomics, deterministic summation order.
+//
+// Work split (canonical form, plan.h):
+//   * a warp owns one ring piece (i3, s) at a time and runs the whole chain for it:
+//       S1  D1[(t,i2),(o1,u)] = x_i3 . G1_s          mma, A fragments loaded from x directly
+//       T1  D1 -> fp16 -> the warp's own shared tile [(t,o1)][(i2,u)]      (__syncwarp only)
+//       S2  D2[(t,o1),(o2,v)] = T1 . G2               mma, A by ldmatrix, B from shared memory
+//       S3  Y[(t,o1),(o2,o3)] += D2 . G3_piece        mma, A = D2 re-packed in registers
+//   * a thread-block cluster of CL CTAs covers all I3*R pieces for one chunk of O2C output
+//     modes o2 (cluster index = o2 chunk).  Warp partials are summed in shared memory, CTA
+//     partials across the cluster through distributed shared memory, and the cluster writes its
+//     slice of y.  Clusters of different o2 chunks repeat S1 (cheap at decode sizes) instead of
+//     reducing through global memory.
+//
+// Replaces the reference's T = 1 kernel tr_ring_fused_v3_kernel (csrc/tr_ring.cu:543-751),
+// which splits pieces over blocks and reduces them with red.global.add into a zeroed
+// workspace finished by the last block.
+#include <cooperative_groups.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "device_util.cuh"
+#include "plan.h"
+
+namespace cg = cooperative_groups;
+
+namespace trr {
+
+struct DecodeParams {
+  const void* x;
+  void* y;
+  const uint2* g1f;
+  const uint2* g2f;
+  const uint2* g3f;
+  int T;
+  int I1, I2, I3, O1, O2, O3, R;
+  int d_in, d_out;
+  long long sx1, sx2, sx3, sy1, sy2, sy3;
+  int KS1, NT1, K2P, KS2, NT2, O3P, NT3, npieces;
+  int MT1;         // m16 tiles of S1 rows (t, i2)
+  int CL;          // CTAs per cluster (pieces split over them)
+  int O2C;         // o2 modes per cluster
+  int warp_bytes;  // per-warp shared area: T1 tile, later the warp's partial Y
+  int off_warps;   // offset of the per-warp areas (after the staged G2 chunk)
+};
+
+template <typename E, int RP, int KS1M, int NT1M, int O2CM, int MAXT>
+__global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams p) {
+  constexpr int NV = RP / 8;
+  constexpr int KS3 = RP >= 16 ? RP / 16 : 1;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int warp = tid >> 5, lane = tid & 31, nwarps = nthr >> 5;
+  const int g = lane >> 2, t4 = lane & 3;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = (int)cluster.block_rank();
+  const int chunk = blockIdx.x / p.CL;
+  const int o2a = chunk * p.O2C;
+  const int o2n = min(p.O2C, p.O2 - o2a);
+  const int pa = (int)((long long)crank * p.npieces / p.CL);
+  const int pb = (int)((long long)(crank + 1) * p.npieces / p.CL);
+  const int T1STR = p.K2P + 8;
+  const int YSTR = O2CM * p.O3P;          // partial Y row: this chunk's (o2, o3)
+  const int rows = p.T * p.O1;            // valid S2 rows (t, o1), <= 16
+  const int s1rows = p.T * p.I2;          // valid S1 rows (t, i2)
+
+  // ---- stage this chunk's G2 fragments: per k-step, O2C*NV contiguous n-tiles
+  {
+    const int per_ks = o2n * NV * 256;
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+    for (int ks = 0; ks < p.KS2; ++ks) {
+      const char* src = reinterpret_cast<const char*>(p.g2f + ((size_t)ks * p.NT2 + o2a * NV) * 32);
+      for (int i = tid * 16; i < per_ks; i += nthr * 16)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s + ks * per_ks + i),
+                     "l"(src + i)
+                     : "memory");
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  }
+  unsigned char* wbase = smem + p.off_warps + warp * p.warp_bytes;
+  __half* t1 = reinterpret_cast<__half*>(wbase);
+  float* yw = reinterpret_cast<float*>(wbase);
+  {  // clear this warp's T1 tile: padding rows (t,o1) >= rows and columns >= I2*RP stay zero
+    uint4* z = reinterpret_cast<uint4*>(wbase);
+    for (int i = lane; i < p.warp_bytes / 16; i += 32) z[i] = make_uint4(0u, 0u, 0u, 0u);
+  }
+
+  float yacc[O2CM][4][4];
+#pragma unroll
+  for (int a = 0; a < O2CM; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) yacc[a][b][c] = 0.f;
+
+  const E* x = static_cast<const E*>(p.x);
+  bool g2_ready = false;
+  const int iters = (pb - pa + nwarps - 1) / nwarps;  // same count in every warp
+  for (int it = 0; it < iters; ++it) {
+    const int pi = pa + warp + it * nwarps;
+    const bool active = pi < pb;
+    const int i3 = active ? pi / p.R : 0, s = active ? pi % p.R : 0;
+    // ---- operands of this piece, all loads issued before any use
+    uint2 g1[KS1M][NT1M];
+#pragma unroll
+    for (int k = 0; k < KS1M; ++k)
+#pragma unroll
+      for (int n = 0; n < NT1M; ++n)
+        g1[k][n] = (active && k < p.KS1 && n < p.NT1)
+                       ? __ldg(p.g1f + (((size_t)s * p.KS1 + k) * p.NT1 + n) * 32 + lane)
+                       : make_uint2(0u, 0u);
+    uint2 b3[KS3][4];
+#pragma unroll
+    for (int k = 0; k < KS3; ++k)
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+        b3[k][n] = (active && n < p.NT3)
+                       ? __ldg(p.g3f + (((size_t)pi * KS3 + k) * p.NT3 + n) * 32 + lane)
+                       : make_uint2(0u, 0u);
+    // x A fragments: rows (t, i2) = 16*mt + g (+8), columns i1 = 16*k + 2*t4 (+1, +8, +9)
+    uint32_t xa[2][KS1M][4];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int k = 0; k < KS1M; ++k)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int r = mt * 16 + g + (q & 1) * 8;
+          const int c = k * 16 + 2 * t4 + (q >> 1) * 8;
+          float lo = 0.f, hi = 0.f;
+          if (active && mt < p.MT1 && k < p.KS1 && r < s1rows) {
+            const int t = r / p.I2, i2 = r - t * p.I2;
+            const E* row = x + (size_t)t * p.d_in + i2 * p.sx2 + i3 * p.sx3;
+            if (c < p.I1) lo = to_f32<E>(row[c * p.sx1]);
+            if (c + 1 < p.I1) hi = to_f32<E>(row[(c + 1) * p.sx1]);
+          }
+          xa[mt][k][q] = pack2<E>(lo, hi);
+        }
+    __syncwarp();
+    // ---- S1 -> T1 (this warp's tile), one n8 column tile at a time
+#pragma unroll
+    for (int n = 0; n < NT1M; ++n) {
+      if (n < p.NT1) {
+        const int col = n * 8 + 2 * t4;
+        const int o1 = col / RP, u = col % RP;
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          if (mt < p.MT1) {
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int k = 0; k < KS1M; ++k)
+              if (k < p.KS1) mma_16816(d, xa[mt][k], g1[k][n].x, g1[k][n].y, E());
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int r = mt * 16 + g + 8 * h;
+              if (r < s1rows) {
+                const int t = r / p.I2, i2 = r - t * p.I2;
+                *reinterpret_cast<__half2*>(t1 + (size_t)(t * p.O1 + o1) * T1STR + i2 * RP + u) =
+                    __floats2half2_rn(d[2 * h], d[2 * h + 1]);
+              }
+            }
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (!g2_ready) {  // the staged G2 chunk: needed from here on, once
+      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+      __syncthreads();
+      g2_ready = true;
+    }
+    // ---- S2 for every o2 of the chunk, A fragments shared across them
+    float d2[O2CM][NV][4];
+#pragma unroll
+    for (int a = 0; a < O2CM; ++a)
+#pragma unroll
+      for (int b = 0; b < NV; ++b)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) d2[a][b][c] = 0.f;
+    const uint2* g2s = reinterpret_cast<const uint2*>(smem) + lane;
+    for (int ks = 0; ks < p.KS2; ++ks) {
+      uint32_t a[4];
+      ldsm_x4(a, t1 + (size_t)(lane & 15) * T1STR + ks * 16 + (lane >> 4) * 8);
+#pragma unroll
+      for (int o = 0; o < O2CM; ++o) {
+        if (o < o2n) {
+#pragma unroll
+          for (int nv = 0; nv < NV; ++nv) {
+            const uint2 b = g2s[((size_t)ks * o2n * NV + o * NV + nv) * 32];
+            mma_16816(d2[o][nv], a, b.x, b.y, __half());
+          }
+        }
+      }
+    }
+    // ---- S3
+#pragma unroll
+    for (int o = 0; o < O2CM; ++o) {
+      if (o < o2n) {
+        if constexpr (RP == 8) {
+          const uint32_t a0 = pack2<__half>(d2[o][0][0], d2[o][0][1]);
+          const uint32_t a1 = pack2<__half>(d2[o][0][2], d2[o][0][3]);
+#pragma unroll
+          for (int n = 0; n < 4; ++n)
+            if (n < p.NT3) mma_1688(yacc[o][n], a0, a1, b3[0][n].x);
+        } else {
+#pragma unroll
+          for (int k = 0; k < KS3; ++k) {
+            uint32_t a[4];
+            a[0] = pack2<__half>(d2[o][2 * k][0], d2[o][2 * k][1]);
+            a[1] = pack2<__half>(d2[o][2 * k][2], d2[o][2 * k][3]);
+            a[2] = pack2<__half>(d2[o][2 * k + 1][0], d2[o][2 * k + 1][1]);
+            a[3] = pack2<__half>(d2[o][2 * k + 1][2], d2[o][2 * k + 1][3]);
+#pragma unroll
+            for (int n = 0; n < 4; ++n)
+              if (n < p.NT3) mma_16816(yacc[o][n], a, b3[k][n].x, b3[k][n].y, __half());
+          }
+        }
+      }
+    }
+    __syncwarp();  // T1 fully read before the next piece overwrites it
+  }
+  if (!g2_ready) {  // warps without pieces still take part in the CTA barrier
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    __syncthreads();
+  }
+
+  // ---- warp partial -> its shared area (rows (t,o1), columns (o2 of chunk, o3))
+  __syncwarp();
+#pragma unroll
+  for (int o = 0; o < O2CM; ++o)
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int r = g + 8 * h;
+        const int col = o * p.O3P + n * 8 + 2 * t4;
+        if (r < rows && n < p.NT3)
+          *reinterpret_cast<float2*>(yw + (size_t)r * YSTR + col) =
+              make_float2(yacc[o][n][2 * h], yacc[o][n][2 * h + 1]);
+      }
+  __syncthreads();
+  // ---- sum the warps (fixed order) into warp 0's area
+  float* ycta = reinterpret_cast<float*>(smem + p.off_warps);
+  const int nel = rows * YSTR;
+  for (int e = tid; e < nel; e += nthr) {
+    float v = 0.f;
+    for (int w = 0; w < nwarps; ++w)
+      v += reinterpret_cast<const float*>(smem + p.off_warps + w * p.warp_bytes)[e];
+    ycta[e] = v;
+  }
+  cluster.sync();
+  // ---- sum the cluster's CTAs (rank order) for this CTA's slice; write y
+  const float* peer[16];
+#pragma unroll
+  for (int r = 0; r < 16; ++r) peer[r] = r < p.CL ? cluster.map_shared_rank(ycta, r) : ycta;
+  const int nout = rows * o2n * p.O3;
+  const int ebeg = (int)((long long)crank * nout / p.CL);
+  const int eend = (int)((long long)(crank + 1) * nout / p.CL);
+  E* y = static_cast<E*>(p.y);
+  for (int e = ebeg + tid; e < eend; e += nthr) {
+    const int o3 = e % p.O3, q = e / p.O3;
+    const int o = q % o2n, r = q / o2n;
+    const int t = r / p.O1, o1 = r - t * p.O1;
+    const int idx = r * YSTR + o * p.O3P + o3;
+    float v[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) v[k] = k < p.CL ? peer[k][idx] : 0.f;
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) sum += v[k];
+    y[(size_t)t * p.d_out + o1 * p.sy1 + (o2a + o) * p.sy2 + o3 * p.sy3] = from_f32<E>(sum);
+  }
+  cluster.sync();  // peers finished reading this CTA's shared memory
+}
+
+// ------------------------------------------------------------------------------------------
+template <typename E, int RP, int KS1M, int NT1M, int O2CM, int MAXT>
+static cudaError_t launch_decode_variant(const DecodeParams& dp, const DecodeGeom& g, int device,
+                                         cudaStream_t st) {
+  auto kern = ring_decode_kernel<E, RP, KS1M, NT1M, O2CM, MAXT>;
+  static bool configured[64] = {};
+  if (device >= 0 && device < 64 && !configured[device]) {
+    int optin = 0;
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    configured[device] = true;
+  }
+  if (g.NW * 32 > MAXT) return cudaErrorInvalidConfiguration;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(g.NOC * g.CL));
+  cfg.blockDim = dim3((unsigned)(g.NW * 32));
+  cfg.dynamicSmemBytes = g.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)g.CL;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, dp);
+}
+
+// Variant = (S1 k-steps, S1 n-tiles) capacity: (1,16) 512 threads, (1,32) 384, (2,32) 256.
+int decode_variant(const Plan& p) {
+  if (p.m.KS1 > 2 || p.m.NT1 > 32 || p.m.RP > 16) return -1;
+  if (p.m.KS1 == 1 && p.m.NT1 <= 16) return 0;
+  if (p.m.KS1 == 1) return 1;
+  return 2;
+}
+
+int decode_max_threads(int variant) { return variant == 0 ? 512 : (variant == 1 ? 384 : 256); }
+
+template <typename E, int RP>
+static cudaError_t launch_decode_rp(const Plan& p, const DecodeParams& dp, const DecodeGeom& g,
+                                    cudaStream_t st) {
+  switch (decode_variant(p)) {
+    case 0: return launch_decode_variant<E, RP, 1, 16, 4, 512>(dp, g, p.device, st);
+    case 1: return launch_decode_variant<E, RP, 1, 32, 4, 384>(dp, g, p.device, st);
+    default: return launch_decode_variant<E, RP, 2, 32, 4, 256>(dp, g, p.device, st);
+  }
+}
+
+template <typename E>
+static cudaError_t launch_decode_e(const Plan& p, const DecodeParams& dp, const DecodeGeom& g,
+                                   cudaStream_t st) {
+  return p.m.RP == 8 ? launch_decode_rp<E, 8>(p, dp, g, st) : launch_decode_rp<E, 16>(p, dp, g, st);
+}
+
+int launch_decode(const Plan& p, const DecodeGeom& g, const void* packed, const void* x,
+                  int64_t T, void* y, void* stream) {
+  const Canon& c = p.c;
+  const MmaLayout& m = p.m;
+  const char* base = static_cast<const char*>(packed);
+  DecodeParams dp;
+  dp.x = x;
+  dp.y = y;
+  dp.g1f = reinterpret_cast<const uint2*>(base + m.off_g1);
+  dp.g2f = reinterpret_cast<const uint2*>(base + m.off_g2);
+  dp.g3f = reinterpret_cast<const uint2*>(base + m.off_g3);
+  dp.T = (int)T;
+  dp.I1 = c.I1; dp.I2 = c.I2; dp.I3 = c.I3;
+  dp.O1 = c.O1; dp.O2 = c.O2; dp.O3 = c.O3;
+  dp.R = c.R;
+  dp.d_in = c.d_in;
+  dp.d_out = c.d_out;
+  dp.sx1 = c.sx1; dp.sx2 = c.sx2; dp.sx3 = c.sx3;
+  dp.sy1 = c.sy1; dp.sy2 = c.sy2; dp.sy3 = c.sy3;
+  dp.KS1 = m.KS1; dp.NT1 = m.NT1; dp.K2P = m.K2P; dp.KS2 = m.KS2; dp.NT2 = m.NT2;
+  dp.O3P = m.O3P; dp.NT3 = m.NT3; dp.npieces = m.npieces;
+  dp.MT1 = g.MT1;
+  dp.CL = g.CL;
+  dp.O2C = g.O2C;
+  dp.warp_bytes = (int)g.warp_bytes;
+  dp.off_warps = (int)g.off_warps;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const cudaError_t e = p.dtype == TR_F16 ? launch_decode_e<__half>(p, dp, g, st)
+                                          : launch_decode_e<__nv_bfloat16>(p, dp, g, st);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("decode kernel launch (chunks=%d CL=%d warps=%d smem=%zu): %s", g.NOC, g.CL, g.NW,
+              g.smem, cudaGetErrorString(e));
+    return TR_ERR_CUDA;
+  }
+  return TR_OK;
+}
+
+}  // namespace trr

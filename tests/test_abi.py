@@ -115,10 +115,12 @@ def test_geometry_and_workspace():
     s = kspec.SPEC_C1
     p = abi.Plan(s.input_modes, s.output_modes, s.rank, abi.TR_F16)
     t = p.tiling(1)
-    assert t.kernel == abi.KERNEL_MMA and t.tokens_per_tile == 1
+    assert t.kernel == abi.KERNEL_DECODE and t.tokens_per_tile == 1
+    assert p.workspace_bytes(1) == 0          # the decode kernel reduces inside its clusters
     assert p.workspace_bytes(0) == 0
-    for T in (1, 8, 32, 33, 1000):
+    for T in (2, 8, 32, 33, 1000):
         t = p.tiling(T)
+        assert t.kernel == abi.KERNEL_MMA
         ws = p.workspace_bytes(T)
         assert (ws > 0) == (t.clusters > 1)
     forced = abi.TrTiling(tokens_per_tile=2, cluster=4, clusters=3, kernel=abi.KERNEL_MMA)

@@ -116,6 +116,39 @@ def test_forced_tilings(golden, R, tiling):
         torch.testing.assert_close(y1, y2, rtol=0, atol=0)
 
 
+# decode kernel geometries: (cluster = CTAs splitting the pieces, clusters = o2 chunks)
+DECODE = [(16, 1), (16, 3), (8, 6), (4, 12), (1, 1), (16, 12), (5, 2), (3, 4)]
+
+
+@pytest.mark.parametrize("R", [8, 16])
+@pytest.mark.parametrize("geom", DECODE)
+def test_decode_geometries(golden, R, geom):
+    key = f"req_r{R}"
+    fn = prepare_optimized(golden_cores(golden, key, torch.float16), kspec.TRSpec(rank=R))
+    assert fn.tiling(1)["kernel"] == abi.KERNEL_DECODE
+    x = t(golden[f"{key}_x_t1"], torch.float16)
+    CL, NOC = geom
+    y1 = fn.call_tiled(x, abi.KERNEL_DECODE, 1, CL, NOC)
+    y2 = fn.call_tiled(x, abi.KERNEL_DECODE, 1, CL, NOC)
+    check_close(y1, golden[f"{key}_yref_t1"], torch.float16)
+    torch.testing.assert_close(y1, y2, rtol=0, atol=0)
+    check_close(y1, fn.call_tiled(x, abi.KERNEL_MMA).double().cpu().numpy(), torch.float16)
+
+
+@pytest.mark.parametrize("name,T", [("k", 1), ("k", 2), ("down", 1), ("gate", 1), ("q", 1)])
+def test_decode_chain_layers(name, T):
+    """Config-4 layer shapes in bf16 at decode sizes (k/v at T = 2 fills the m16 tile with two
+    tokens and two S1 row tiles), against the oracle."""
+    s = kspec.SPEC_C4[name]
+    cores = kspec.baseline_cores(s, seed=5, dtype=torch.bfloat16, device=DEV)
+    fn = prepare_optimized(cores, s)
+    x = kspec.baseline_x(s, T, seed=5, dtype=torch.bfloat16, device=DEV)
+    assert fn.tiling(T)["kernel"] == abi.KERNEL_DECODE
+    ref = oracle.tr_forward_reference(x.float().cpu().numpy(),
+                                      [c.float().cpu().numpy() for c in cores])
+    check_close(fn(x), ref, torch.bfloat16)
+
+
 @pytest.mark.parametrize("name", ["c3", "c5", "c4_q", "c4_k", "c4_gate", "c4_down"])
 def test_baseline_configs_bf16(golden_baseline, name):
     meta, vec = golden_baseline

@@ -36,8 +36,8 @@ def test_noalloc_matches_tr_forward(spec, dtype, code):
     stream = torch.cuda.current_stream().cuda_stream
     for T in (1, 8, 3):
         x = kspec.baseline_x(spec, T, seed=1, dtype=dtype, device=device)
-        tiling = plan.tiling(T)
-        assert tiling.clusters > 1, "the case must exercise the scratch reduction"
+        mma = abi.TrTiling(kernel=abi.KERNEL_MMA)
+        assert plan.workspace_bytes(T, mma) > 0, "the case must exercise the scratch reduction"
         ws_bytes = plan.workspace_bytes(T)
         ws = torch.zeros(max(ws_bytes, 16), dtype=torch.uint8, device=device)
         y_ref = torch.empty(T, spec.out_features, dtype=dtype, device=device)

@@ -257,7 +257,10 @@ int resolve_decode_geom(const Plan& p, int64_t T, const tr_tiling* f, DecodeGeom
     g->O2C = O2C;
     g->NOC = NOC;
     g->off_warps = align_up((size_t)m.KS2 * O2C * (m.RP / 8) * 256, 128);
-    g->smem = g->off_warps + (size_t)g->NW * g->warp_bytes;
+    g->off_recv = align_up(g->off_warps + (size_t)g->NW * g->warp_bytes, 128);
+    const size_t nout = (size_t)T * c.O1 * O2C * c.O3;
+    const size_t slice = (nout + CL - 1) / CL;
+    g->smem = align_up(g->off_recv + (size_t)CL * slice * 4, 128);
     if (g->smem <= p.smem_optin) break;
     if (g->NW > 4) {
       g->NW = std::max(4, g->NW / 2);

@@ -95,6 +95,7 @@ struct DecodeGeom {
   int MT1;       // m16 tiles of S1 rows (t, i2): 1 or 2
   size_t warp_bytes;  // per-warp shared area (T1 tile, then the warp's partial Y)
   size_t off_warps;   // after the staged G2 chunk
+  size_t off_recv;    // cluster-reduction receive slots, after the warp areas
   size_t smem;
 };
 

@@ -24,31 +24,32 @@
 
 #include "device_util.cuh"
 #include "plan.h"
+#include "shapes.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace trr {
 
+template <class S>
 struct DecodeParams {
+  S sh;            // shape: compile-time (FixedShape) or runtime (DynShape)
   const void* x;
   void* y;
   const uint2* g1f;
   const uint2* g2f;
   const uint2* g3f;
   int T;
-  int I1, I2, I3, O1, O2, O3, R;
-  int d_in, d_out;
-  long long sx1, sx2, sx3, sy1, sy2, sy3;
-  int KS1, NT1, K2P, KS2, NT2, O3P, NT3, npieces;
   int MT1;         // m16 tiles of S1 rows (t, i2)
   int CL;          // CTAs per cluster (pieces split over them)
   int O2C;         // o2 modes per cluster
   int warp_bytes;  // per-warp shared area: T1 tile, later the warp's partial Y
   int off_warps;   // offset of the per-warp areas (after the staged G2 chunk)
+  int off_recv;    // receive slots of the cluster reduction (CL x slice, fp32)
 };
 
-template <typename E, int RP, int KS1M, int NT1M, int O2CM, int MAXT>
-__global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams p) {
+template <class S, typename E, int RP, int KS1M, int NT1M, int O2CM, int MAXT>
+__global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams<S> p) {
+  const S& sh = p.sh;
   constexpr int NV = RP / 8;
   constexpr int KS3 = RP >= 16 ? RP / 16 : 1;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -57,22 +58,24 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
   const int g = lane >> 2, t4 = lane & 3;
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
+  // announce that this CTA runs; the matching wait precedes the first remote store
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
   const int chunk = blockIdx.x / p.CL;
   const int o2a = chunk * p.O2C;
-  const int o2n = min(p.O2C, p.O2 - o2a);
-  const int pa = (int)((long long)crank * p.npieces / p.CL);
-  const int pb = (int)((long long)(crank + 1) * p.npieces / p.CL);
-  const int T1STR = p.K2P + 8;
-  const int YSTR = O2CM * p.O3P;          // partial Y row: this chunk's (o2, o3)
-  const int rows = p.T * p.O1;            // valid S2 rows (t, o1), <= 16
-  const int s1rows = p.T * p.I2;          // valid S1 rows (t, i2)
+  const int o2n = min(p.O2C, sh.O2 - o2a);
+  const int pa = (int)((long long)crank * sh.npieces / p.CL);
+  const int pb = (int)((long long)(crank + 1) * sh.npieces / p.CL);
+  const int T1STR = sh.K2P + 8;
+  const int YSTR = O2CM * sh.O3P;          // partial Y row: this chunk's (o2, o3)
+  const int rows = p.T * sh.O1;            // valid S2 rows (t, o1), <= 16
+  const int s1rows = p.T * sh.I2;          // valid S1 rows (t, i2)
 
   // ---- stage this chunk's G2 fragments: per k-step, O2C*NV contiguous n-tiles
   {
     const int per_ks = o2n * NV * 256;
     const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
-    for (int ks = 0; ks < p.KS2; ++ks) {
-      const char* src = reinterpret_cast<const char*>(p.g2f + ((size_t)ks * p.NT2 + o2a * NV) * 32);
+    for (int ks = 0; ks < sh.KS2; ++ks) {
+      const char* src = reinterpret_cast<const char*>(p.g2f + ((size_t)ks * sh.NT2 + o2a * NV) * 32);
       for (int i = tid * 16; i < per_ks; i += nthr * 16)
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s + ks * per_ks + i),
                      "l"(src + i)
@@ -102,23 +105,23 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
   for (int it = 0; it < iters; ++it) {
     const int pi = pa + warp + it * nwarps;
     const bool active = pi < pb;
-    const int i3 = active ? pi / p.R : 0, s = active ? pi % p.R : 0;
+    const int i3 = active ? pi / sh.R : 0, s = active ? pi % sh.R : 0;
     // ---- operands of this piece, all loads issued before any use
     uint2 g1[KS1M][NT1M];
 #pragma unroll
     for (int k = 0; k < KS1M; ++k)
 #pragma unroll
       for (int n = 0; n < NT1M; ++n)
-        g1[k][n] = (active && k < p.KS1 && n < p.NT1)
-                       ? __ldg(p.g1f + (((size_t)s * p.KS1 + k) * p.NT1 + n) * 32 + lane)
+        g1[k][n] = (active && k < sh.KS1 && n < sh.NT1)
+                       ? __ldg(p.g1f + (((size_t)s * sh.KS1 + k) * sh.NT1 + n) * 32 + lane)
                        : make_uint2(0u, 0u);
     uint2 b3[KS3][4];
 #pragma unroll
     for (int k = 0; k < KS3; ++k)
 #pragma unroll
       for (int n = 0; n < 4; ++n)
-        b3[k][n] = (active && n < p.NT3)
-                       ? __ldg(p.g3f + (((size_t)pi * KS3 + k) * p.NT3 + n) * 32 + lane)
+        b3[k][n] = (active && n < sh.NT3)
+                       ? __ldg(p.g3f + (((size_t)pi * KS3 + k) * sh.NT3 + n) * 32 + lane)
                        : make_uint2(0u, 0u);
     // x A fragments: rows (t, i2) = 16*mt + g (+8), columns i1 = 16*k + 2*t4 (+1, +8, +9)
     uint32_t xa[2][KS1M][4];
@@ -131,11 +134,11 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
           const int r = mt * 16 + g + (q & 1) * 8;
           const int c = k * 16 + 2 * t4 + (q >> 1) * 8;
           float lo = 0.f, hi = 0.f;
-          if (active && mt < p.MT1 && k < p.KS1 && r < s1rows) {
-            const int t = r / p.I2, i2 = r - t * p.I2;
-            const E* row = x + (size_t)t * p.d_in + i2 * p.sx2 + i3 * p.sx3;
-            if (c < p.I1) lo = to_f32<E>(row[c * p.sx1]);
-            if (c + 1 < p.I1) hi = to_f32<E>(row[(c + 1) * p.sx1]);
+          if (active && mt < p.MT1 && k < sh.KS1 && r < s1rows) {
+            const int t = r / sh.I2, i2 = r - t * sh.I2;
+            const E* row = x + (size_t)t * sh.d_in + i2 * sh.sx2 + i3 * sh.sx3;
+            if (c < sh.I1) lo = to_f32<E>(row[c * sh.sx1]);
+            if (c + 1 < sh.I1) hi = to_f32<E>(row[(c + 1) * sh.sx1]);
           }
           xa[mt][k][q] = pack2<E>(lo, hi);
         }
@@ -143,7 +146,7 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
     // ---- S1 -> T1 (this warp's tile), one n8 column tile at a time
 #pragma unroll
     for (int n = 0; n < NT1M; ++n) {
-      if (n < p.NT1) {
+      if (n < sh.NT1) {
         const int col = n * 8 + 2 * t4;
         const int o1 = col / RP, u = col % RP;
 #pragma unroll
@@ -152,13 +155,13 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
             float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int k = 0; k < KS1M; ++k)
-              if (k < p.KS1) mma_16816(d, xa[mt][k], g1[k][n].x, g1[k][n].y, E());
+              if (k < sh.KS1) mma_16816(d, xa[mt][k], g1[k][n].x, g1[k][n].y, E());
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               const int r = mt * 16 + g + 8 * h;
               if (r < s1rows) {
-                const int t = r / p.I2, i2 = r - t * p.I2;
-                *reinterpret_cast<__half2*>(t1 + (size_t)(t * p.O1 + o1) * T1STR + i2 * RP + u) =
+                const int t = r / sh.I2, i2 = r - t * sh.I2;
+                *reinterpret_cast<__half2*>(t1 + (size_t)(t * sh.O1 + o1) * T1STR + i2 * RP + u) =
                     __floats2half2_rn(d[2 * h], d[2 * h + 1]);
               }
             }
@@ -181,7 +184,7 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
 #pragma unroll
         for (int c = 0; c < 4; ++c) d2[a][b][c] = 0.f;
     const uint2* g2s = reinterpret_cast<const uint2*>(smem) + lane;
-    for (int ks = 0; ks < p.KS2; ++ks) {
+    for (int ks = 0; ks < sh.KS2; ++ks) {
       uint32_t a[4];
       ldsm_x4(a, t1 + (size_t)(lane & 15) * T1STR + ks * 16 + (lane >> 4) * 8);
 #pragma unroll
@@ -204,7 +207,7 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
           const uint32_t a1 = pack2<__half>(d2[o][0][2], d2[o][0][3]);
 #pragma unroll
           for (int n = 0; n < 4; ++n)
-            if (n < p.NT3) mma_1688(yacc[o][n], a0, a1, b3[0][n].x);
+            if (n < sh.NT3) mma_1688(yacc[o][n], a0, a1, b3[0][n].x);
         } else {
 #pragma unroll
           for (int k = 0; k < KS3; ++k) {
@@ -215,7 +218,7 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
             a[3] = pack2<__half>(d2[o][2 * k + 1][2], d2[o][2 * k + 1][3]);
 #pragma unroll
             for (int n = 0; n < 4; ++n)
-              if (n < p.NT3) mma_16816(yacc[o][n], a, b3[k][n].x, b3[k][n].y, __half());
+              if (n < sh.NT3) mma_16816(yacc[o][n], a, b3[k][n].x, b3[k][n].y, __half());
           }
         }
       }
@@ -236,51 +239,48 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int r = g + 8 * h;
-        const int col = o * p.O3P + n * 8 + 2 * t4;
-        if (r < rows && n < p.NT3)
+        const int col = o * sh.O3P + n * 8 + 2 * t4;
+        if (r < rows && n < sh.NT3)
           *reinterpret_cast<float2*>(yw + (size_t)r * YSTR + col) =
               make_float2(yacc[o][n][2 * h], yacc[o][n][2 * h + 1]);
       }
   __syncthreads();
-  // ---- sum the warps (fixed order) into warp 0's area
-  float* ycta = reinterpret_cast<float*>(smem + p.off_warps);
-  const int nel = rows * YSTR;
-  for (int e = tid; e < nel; e += nthr) {
+  // ---- push: sum the warps (fixed order) for each output of the chunk and store the CTA's
+  // partial into the owning CTA's receive slot (distributed shared memory).  Output e of the
+  // chunk, e = (row, o2, o3) with o3 fastest, belongs to cluster rank e / SL.
+  const int nout = rows * o2n * sh.O3;
+  const int SL = (nout + p.CL - 1) / p.CL;
+  float* recv = reinterpret_cast<float*>(smem + p.off_recv);
+  asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");  // every peer has started
+  for (int e = tid; e < nout; e += nthr) {
+    const int o3 = e % sh.O3, q = e / sh.O3;
+    const int o = q % o2n, r = q / o2n;
+    const int idx = r * YSTR + o * sh.O3P + o3;
     float v = 0.f;
     for (int w = 0; w < nwarps; ++w)
-      v += reinterpret_cast<const float*>(smem + p.off_warps + w * p.warp_bytes)[e];
-    ycta[e] = v;
+      v += reinterpret_cast<const float*>(smem + p.off_warps + w * p.warp_bytes)[idx];
+    const int owner = e / SL;
+    cluster.map_shared_rank(recv, owner)[crank * SL + (e - owner * SL)] = v;
   }
-  cluster.sync();
-  // ---- sum the cluster's CTAs (rank order) for this CTA's slice; write y
-  const float* peer[16];
-#pragma unroll
-  for (int r = 0; r < 16; ++r) peer[r] = r < p.CL ? cluster.map_shared_rank(ycta, r) : ycta;
-  const int nout = rows * o2n * p.O3;
-  const int ebeg = (int)((long long)crank * nout / p.CL);
-  const int eend = (int)((long long)(crank + 1) * nout / p.CL);
+  cluster.sync();  // all partials have landed in their owners' receive slots
+  // ---- own slice: add the CL partials in rank order and write y
   E* y = static_cast<E*>(p.y);
+  const int ebeg = crank * SL, eend = min(nout, ebeg + SL);
   for (int e = ebeg + tid; e < eend; e += nthr) {
-    const int o3 = e % p.O3, q = e / p.O3;
-    const int o = q % o2n, r = q / o2n;
-    const int t = r / p.O1, o1 = r - t * p.O1;
-    const int idx = r * YSTR + o * p.O3P + o3;
-    float v[16];
-#pragma unroll
-    for (int k = 0; k < 16; ++k) v[k] = k < p.CL ? peer[k][idx] : 0.f;
     float sum = 0.f;
-#pragma unroll
-    for (int k = 0; k < 16; ++k) sum += v[k];
-    y[(size_t)t * p.d_out + o1 * p.sy1 + (o2a + o) * p.sy2 + o3 * p.sy3] = from_f32<E>(sum);
+    for (int k = 0; k < p.CL; ++k) sum += recv[k * SL + (e - ebeg)];
+    const int o3 = e % sh.O3, q = e / sh.O3;
+    const int o = q % o2n, r = q / o2n;
+    const int t = r / sh.O1, o1 = r - t * sh.O1;
+    y[(size_t)t * sh.d_out + o1 * sh.sy1 + (o2a + o) * sh.sy2 + o3 * sh.sy3] = from_f32<E>(sum);
   }
-  cluster.sync();  // peers finished reading this CTA's shared memory
 }
 
 // ------------------------------------------------------------------------------------------
-template <typename E, int RP, int KS1M, int NT1M, int O2CM, int MAXT>
-static cudaError_t launch_decode_variant(const DecodeParams& dp, const DecodeGeom& g, int device,
-                                         cudaStream_t st) {
-  auto kern = ring_decode_kernel<E, RP, KS1M, NT1M, O2CM, MAXT>;
+template <class S, typename E, int RP, int KS1M, int NT1M, int O2CM, int MAXT>
+static cudaError_t launch_decode_variant(const DecodeParams<S>& dp, const DecodeGeom& g,
+                                         int device, cudaStream_t st) {
+  auto kern = ring_decode_kernel<S, E, RP, KS1M, NT1M, O2CM, MAXT>;
   static bool configured[64] = {};
   if (device >= 0 && device < 64 && !configured[device]) {
     int optin = 0;
@@ -317,51 +317,92 @@ int decode_variant(const Plan& p) {
 
 int decode_max_threads(int variant) { return variant == 0 ? 512 : (variant == 1 ? 384 : 256); }
 
-template <typename E, int RP>
-static cudaError_t launch_decode_rp(const Plan& p, const DecodeParams& dp, const DecodeGeom& g,
-                                    cudaStream_t st) {
-  switch (decode_variant(p)) {
-    case 0: return launch_decode_variant<E, RP, 1, 16, 4, 512>(dp, g, p.device, st);
-    case 1: return launch_decode_variant<E, RP, 1, 32, 4, 384>(dp, g, p.device, st);
-    default: return launch_decode_variant<E, RP, 2, 32, 4, 256>(dp, g, p.device, st);
-  }
-}
-
-template <typename E>
-static cudaError_t launch_decode_e(const Plan& p, const DecodeParams& dp, const DecodeGeom& g,
-                                   cudaStream_t st) {
-  return p.m.RP == 8 ? launch_decode_rp<E, 8>(p, dp, g, st) : launch_decode_rp<E, 16>(p, dp, g, st);
-}
-
-int launch_decode(const Plan& p, const DecodeGeom& g, const void* packed, const void* x,
-                  int64_t T, void* y, void* stream) {
-  const Canon& c = p.c;
-  const MmaLayout& m = p.m;
+template <class S>
+static void fill_common(DecodeParams<S>& dp, const Plan& p, const DecodeGeom& g,
+                        const void* packed, const void* x, int64_t T, void* y) {
   const char* base = static_cast<const char*>(packed);
-  DecodeParams dp;
   dp.x = x;
   dp.y = y;
-  dp.g1f = reinterpret_cast<const uint2*>(base + m.off_g1);
-  dp.g2f = reinterpret_cast<const uint2*>(base + m.off_g2);
-  dp.g3f = reinterpret_cast<const uint2*>(base + m.off_g3);
+  dp.g1f = reinterpret_cast<const uint2*>(base + p.m.off_g1);
+  dp.g2f = reinterpret_cast<const uint2*>(base + p.m.off_g2);
+  dp.g3f = reinterpret_cast<const uint2*>(base + p.m.off_g3);
   dp.T = (int)T;
-  dp.I1 = c.I1; dp.I2 = c.I2; dp.I3 = c.I3;
-  dp.O1 = c.O1; dp.O2 = c.O2; dp.O3 = c.O3;
-  dp.R = c.R;
-  dp.d_in = c.d_in;
-  dp.d_out = c.d_out;
-  dp.sx1 = c.sx1; dp.sx2 = c.sx2; dp.sx3 = c.sx3;
-  dp.sy1 = c.sy1; dp.sy2 = c.sy2; dp.sy3 = c.sy3;
-  dp.KS1 = m.KS1; dp.NT1 = m.NT1; dp.K2P = m.K2P; dp.KS2 = m.KS2; dp.NT2 = m.NT2;
-  dp.O3P = m.O3P; dp.NT3 = m.NT3; dp.npieces = m.npieces;
   dp.MT1 = g.MT1;
   dp.CL = g.CL;
   dp.O2C = g.O2C;
   dp.warp_bytes = (int)g.warp_bytes;
   dp.off_warps = (int)g.off_warps;
+  dp.off_recv = (int)g.off_recv;
+}
+
+DynShape dyn_shape(const Plan& p) {
+  const Canon& c = p.c;
+  const MmaLayout& m = p.m;
+  DynShape d;
+  d.I1 = c.I1; d.I2 = c.I2; d.I3 = c.I3;
+  d.O1 = c.O1; d.O2 = c.O2; d.O3 = c.O3;
+  d.R = c.R;
+  d.d_in = c.d_in;
+  d.d_out = c.d_out;
+  d.sx1 = c.sx1; d.sx2 = c.sx2; d.sx3 = c.sx3;
+  d.sy1 = c.sy1; d.sy2 = c.sy2; d.sy3 = c.sy3;
+  d.KS1 = m.KS1; d.NT1 = m.NT1; d.K2P = m.K2P; d.KS2 = m.KS2; d.NT2 = m.NT2;
+  d.O3P = m.O3P; d.NT3 = m.NT3; d.npieces = m.npieces;
+  d.xm1 = p.spec.input_modes[1]; d.xm2 = p.spec.input_modes[2];
+  d.ym1 = p.spec.output_modes[1]; d.ym2 = p.spec.output_modes[2];
+  d.role0 = c.role[0]; d.role1 = c.role[1]; d.role2 = c.role[2];
+  return d;
+}
+
+template <class S>
+static bool shape_matches(const Plan& p) {
+  return p.spec.input_modes[0] == S::in0 && p.spec.input_modes[1] == S::in1 &&
+         p.spec.input_modes[2] == S::in2 && p.spec.output_modes[0] == S::on0 &&
+         p.spec.output_modes[1] == S::on1 && p.spec.output_modes[2] == S::on2 &&
+         p.spec.rank == S::R && p.c.role[0] == S::role0 && p.c.role[1] == S::role1;
+}
+
+template <class S, typename E>
+static cudaError_t launch_decode_fixed(const Plan& p, const DecodeGeom& g, const void* packed,
+                                       const void* x, int64_t T, void* y, cudaStream_t st) {
+  DecodeParams<S> dp;
+  fill_common(dp, p, g, packed, x, T, y);
+  constexpr int MAXT = (S::KS1 == 1 && S::NT1 <= 16) ? 512 : (S::KS1 == 1 ? 384 : 256);
+  return launch_decode_variant<S, E, S::RPc, S::KS1, S::NT1, 4, MAXT>(dp, g, p.device, st);
+}
+
+template <typename E, int RP>
+static cudaError_t launch_decode_dyn(const Plan& p, const DecodeGeom& g, const void* packed,
+                                     const void* x, int64_t T, void* y, cudaStream_t st) {
+  DecodeParams<DynShape> dp;
+  dp.sh = dyn_shape(p);
+  fill_common(dp, p, g, packed, x, T, y);
+  switch (decode_variant(p)) {
+    case 0: return launch_decode_variant<DynShape, E, RP, 1, 16, 4, 512>(dp, g, p.device, st);
+    case 1: return launch_decode_variant<DynShape, E, RP, 1, 32, 4, 384>(dp, g, p.device, st);
+    default: return launch_decode_variant<DynShape, E, RP, 2, 32, 4, 256>(dp, g, p.device, st);
+  }
+}
+
+template <typename E>
+static cudaError_t launch_decode_e(const Plan& p, const DecodeGeom& g, const void* packed,
+                                   const void* x, int64_t T, void* y, cudaStream_t st) {
+#define TRR_TRY_FIXED(a, b, c, d, e, f, r, X, Y)                                         \
+  if (shape_matches<FixedShape<a, b, c, d, e, f, r, X, Y>>(p))                           \
+    return launch_decode_fixed<FixedShape<a, b, c, d, e, f, r, X, Y>, E>(p, g, packed, x, T, \
+                                                                         y, st);
+  TRR_FIXED_SHAPES(TRR_TRY_FIXED)
+#undef TRR_TRY_FIXED
+  return p.m.RP == 8 ? launch_decode_dyn<E, 8>(p, g, packed, x, T, y, st)
+                     : launch_decode_dyn<E, 16>(p, g, packed, x, T, y, st);
+}
+
+int launch_decode(const Plan& p, const DecodeGeom& g, const void* packed, const void* x,
+                  int64_t T, void* y, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const cudaError_t e = p.dtype == TR_F16 ? launch_decode_e<__half>(p, dp, g, st)
-                                          : launch_decode_e<__nv_bfloat16>(p, dp, g, st);
+  const cudaError_t e = p.dtype == TR_F16
+                            ? launch_decode_e<__half>(p, g, packed, x, T, y, st)
+                            : launch_decode_e<__nv_bfloat16>(p, g, packed, x, T, y, st);
   if (e != cudaSuccess) {
     cudaGetLastError();
     set_error("decode kernel launch (chunks=%d CL=%d warps=%d smem=%zu): %s", g.NOC, g.CL, g.NW,

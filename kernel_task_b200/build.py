@@ -19,7 +19,8 @@ INCLUDE = ROOT / "include"
 LIB = PKG / "libtrring.so"
 EXT = PKG / "_trring_torch.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CUDA_SOURCES = ["plan.cpp", "pack.cu", "ring_generic.cu", "ring_mma.cu", "ring_decode.cu"]
+CUDA_SOURCES = ["plan.cpp", "pack.cu", "ring_generic.cu", "ring_mma.cu", "ring_decode.cu",
+                "ring_tc05.cu"]
 
 
 def _nvcc() -> str:

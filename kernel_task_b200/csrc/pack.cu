@@ -121,6 +121,49 @@ __global__ void pack_mma_kernel(CoreView<E> c0, CoreView<E> c1, CoreView<E> c2, 
   }
 }
 
+// Byte offset of element (row r, column k) in a K-major UMMA tile with K columns: 8x8 core
+// matrices of 128 contiguous bytes, K chunks 128 B apart (LBO), row groups K/8*128 B apart (SBO).
+__host__ __device__ inline size_t umma_kmajor_offset(int r, int k, int K) {
+  return (size_t)(r >> 3) * (K >> 3) * 128 + (size_t)(k >> 3) * 128 + (r & 7) * 16 + (k & 7) * 2;
+}
+
+struct TcPackDims {
+  int I2, I3, O2, O3, R, RP, K2P, O2G, NG, N2, N3P, K3P, npieces;
+};
+
+// tcgen05 B operands (fp16): B2 per o2 group [N2 rows (o2, v)] x [K2P (i2, u)] and B3 per piece
+// [N3P rows o3] x [K3P v]; zero where a padded index has no core entry.
+template <typename E>
+__global__ void pack_tc_kernel(CoreView<E> c1, CoreView<E> c2, TcPackDims d, unsigned char* b2,
+                               unsigned char* b3, size_t n2, size_t n3) {
+  const size_t total = n2 + n3;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    float v;
+    unsigned char* dst;
+    if (idx < n2) {
+      const int k = (int)(idx % d.K2P);
+      size_t q = idx / d.K2P;
+      const int n = (int)(q % d.N2);
+      const int grp = (int)(q / d.N2);
+      const int o2 = grp * d.O2G + n / d.RP, vv = n % d.RP;
+      const int i2 = k / d.RP, u = k % d.RP;
+      v = (o2 < d.O2 && vv < d.R && i2 < d.I2 && u < d.R) ? c1.at(u, o2, i2, vv) : 0.f;
+      dst = b2 + (size_t)grp * d.N2 * d.K2P * 2 + umma_kmajor_offset(n, k, d.K2P);
+    } else {
+      const size_t e = idx - n2;
+      const int k = (int)(e % d.K3P);
+      size_t q = e / d.K3P;
+      const int n = (int)(q % d.N3P);
+      const int piece = (int)(q / d.N3P);
+      const int i3 = piece / d.R, s = piece % d.R;
+      v = (n < d.O3 && k < d.R) ? c2.at(k, n, i3, s) : 0.f;
+      dst = b3 + (size_t)piece * d.N3P * d.K3P * 2 + umma_kmajor_offset(n, k, d.K3P);
+    }
+    *reinterpret_cast<__half*>(dst) = __float2half_rn(v);
+  }
+}
+
 template <typename E>
 static int pack_typed(const Plan& p, const void* const cores[3], void* packed, cudaStream_t st) {
   const Canon& c = p.c;
@@ -148,6 +191,17 @@ static int pack_typed(const Plan& p, const void* const cores[3], void* packed, c
           v[0], v[1], v[2], d, reinterpret_cast<uint2*>(base + m.off_g1),
           reinterpret_cast<uint2*>(base + m.off_g2), reinterpret_cast<uint2*>(base + m.off_g3),
           n1, n2, n3);
+      if (p.tc_ok) {
+        const TcLayout& t = p.t;
+        TcPackDims td{c.I2, c.I3, c.O2, c.O3, c.R, m.RP, m.K2P, t.O2G, t.NG, t.N2, t.N3P, t.K3P,
+                      m.npieces};
+        const size_t tn2 = (size_t)t.NG * t.N2 * m.K2P;
+        const size_t tn3 = (size_t)m.npieces * t.N3P * t.K3P;
+        const int tb = (int)std::min<size_t>((tn2 + tn3 + 255) / 256, 4096);
+        pack_tc_kernel<E><<<tb, 256, 0, st>>>(
+            v[1], v[2], td, reinterpret_cast<unsigned char*>(base + t.off_b2),
+            reinterpret_cast<unsigned char*>(base + t.off_b3), tn2, tn3);
+      }
     }
   }
   if (!done) {

@@ -93,6 +93,82 @@ static void build_mma_layout(Plan* p) {
   m.off_g3 = align_up(m.off_g2 + m.bytes_g2, 256);
 }
 
+// Shared memory of one tcgen05 CTA (ring_tc05.cu):
+//   [x slice MT1*16 x (K1P+8)] [A2 x NA2] [G2 group] [A3 x 2] [G1 frags x 2] [G3 piece x 2]
+//   [mbarriers, TMEM slot, flags: 256 B]; the partial y (128 x O2G*O3 fp32) reuses offset 0.
+struct TcSmem {
+  size_t off_xs, off_a2, a2_bytes, off_b2, off_a3, off_g1, off_bar, total;
+};
+
+static TcSmem tc_smem(const Plan& p, int MT1, int NA2, int O2G) {
+  const MmaLayout& m = p.m;
+  const TcLayout& t = p.t;
+  TcSmem s;
+  const size_t xs = (size_t)MT1 * 16 * (m.KS1 * 16 + 8) * 2;
+  s.a2_bytes = (size_t)16 * (m.K2P / 8) * 144;
+  const size_t b2 = (size_t)O2G * m.RP * m.K2P * 2;
+  const size_t a3 = (size_t)O2G * 128 * t.K3P * 2;
+  const size_t g1 = (size_t)m.KS1 * m.NT1 * 256;
+  const size_t b3 = (size_t)t.N3P * t.K3P * 2;
+  s.off_xs = 0;
+  s.off_a2 = align_up(xs, 128);
+  s.off_b2 = align_up(s.off_a2 + NA2 * s.a2_bytes, 128);
+  s.off_a3 = align_up(s.off_b2 + b2, 128);
+  s.off_g1 = align_up(s.off_a3 + 2 * a3, 128);
+  const size_t main = s.off_g1 + 4 * g1 + 4 * b3;  // G1 and G3 rings of depth 4
+  const size_t ys = (size_t)128 * ((O2G * p.c.O3) | 1) * 4;
+  s.off_bar = align_up(std::max(main, ys), 128);
+  s.total = s.off_bar + 256;
+  return s;
+}
+
+// tcgen05 operand layout (appended to the mma layout in the packed buffer).  O2 is split into
+// NG groups so that a CTA's TMEM holds two S2 accumulators (N2 columns each) and the S3
+// accumulators of its group (O2G x N3P columns) within 512 columns.
+static void build_tc_layout(Plan* p) {
+  const Canon& c = p->c;
+  const MmaLayout& m = p->m;
+  TcLayout& t = p->t;
+  t.N3P = ceil_div(c.O3, 16) * 16;
+  t.K3P = std::max(16, m.RP);
+  const int per_o2 = 2 * m.RP + t.N3P;
+  int o2g_max = std::min(512 / per_o2, 256 / m.RP);
+  if (o2g_max < 1) {
+    p->tc_ok = 0;
+    return;
+  }
+  t.NG = ceil_div(c.O2, o2g_max);
+  t.O2G = ceil_div(c.O2, t.NG);
+  if (m.RP == 8 && (t.O2G & 1)) t.O2G += 1;  // S2's N = O2G*8 must be a multiple of 16
+  t.NG = ceil_div(c.O2, t.O2G);
+  t.N2 = t.O2G * m.RP;
+  const int need = t.N2 * 2 + t.O2G * t.N3P;
+  t.tmem_cols = 32;
+  while (t.tmem_cols < need) t.tmem_cols *= 2;
+  // shrink the groups until the worst-case (TT = 128/O1) shared-memory footprint fits with a
+  // single A2 buffer (resolve_tc_geom takes two when they fit)
+  const int TTw = std::max(1, 128 / std::max(1, c.O1));
+  const int MT1w = ceil_div(TTw * c.I2, 16);
+  for (;;) {
+    if (tc_smem(*p, MT1w, 1, t.O2G).total <= p->smem_optin) break;
+    const int step = (m.RP == 8) ? 2 : 1;
+    if (t.O2G - step < 1) {
+      p->tc_ok = 0;
+      return;
+    }
+    t.O2G -= step;
+  }
+  t.NG = ceil_div(c.O2, t.O2G);
+  t.N2 = t.O2G * m.RP;
+  t.tmem_cols = 32;
+  while (t.tmem_cols < t.N2 * 2 + t.O2G * t.N3P) t.tmem_cols *= 2;
+  t.bytes_b2_group = (size_t)t.N2 * m.K2P * 2;
+  t.bytes_b3_piece = (size_t)t.N3P * t.K3P * 2;
+  t.off_b2 = align_up(m.off_g3 + m.bytes_g3, 256);
+  t.off_b3 = align_up(t.off_b2 + (size_t)t.NG * t.bytes_b2_group, 256);
+  p->tc_ok = p->mma_ok && c.O1 <= 128 && t.tmem_cols <= 512 && t.N3P <= 256;
+}
+
 static void build_generic_layout(Plan* p) {
   const Canon& c = p->c;
   GenericLayout& g = p->g;
@@ -275,6 +351,74 @@ int resolve_decode_geom(const Plan& p, int64_t T, const tr_tiling* f, DecodeGeom
   return TR_OK;
 }
 
+// tcgen05 geometry: row tiles of TT tokens (TT*O1 <= 128), NG o2 groups, NJ = CL*NC CTAs over
+// the pieces of each (tile, group).
+int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* f, TcGeom* g) {
+  const Canon& c = p.c;
+  const MmaLayout& m = p.m;
+  const TcLayout& t = p.t;
+  if (!p.tc_ok) {
+    set_error("tcgen05 kernel does not support this spec/dtype");
+    return TR_ERR_UNSUPPORTED;
+  }
+  int TT = (f && f->tokens_per_tile > 0) ? f->tokens_per_tile : std::max(1, 128 / c.O1);
+  if (TT > T) TT = (int)T;
+  if (TT < 1) TT = 1;
+  if (TT * c.O1 > 128) {
+    set_error("tokens_per_tile=%d x O1=%d exceeds the 128-row tile", TT, c.O1);
+    return TR_ERR_INVALID;
+  }
+  g->TT = TT;
+  g->ntiles = (int)((T + TT - 1) / TT);
+  g->MT1 = ceil_div(TT * c.I2, 16);
+  int CL, NC;
+  if (f && f->cluster > 0) {
+    CL = f->cluster;
+    NC = f->clusters > 0 ? f->clusters : 1;
+  } else {
+    const long long cols = (long long)g->ntiles * t.NG;
+    int NJ = cols >= p.num_sms ? 1 : (int)std::max<long long>(1, p.num_sms / cols);
+    NJ = std::min(NJ, m.npieces);
+    CL = std::min(8, NJ);
+    NC = std::max(1, NJ / CL);
+  }
+  if (CL < 1 || CL > 16 || NC < 1 || (long long)CL * NC > m.npieces) {
+    set_error("cluster=%d clusters=%d invalid for %d pieces", CL, NC, m.npieces);
+    return TR_ERR_INVALID;
+  }
+  g->CL = CL;
+  g->NC = NC;
+  g->NI3L = 1;
+  TcSmem sm = tc_smem(p, g->MT1, 2, t.O2G);
+  g->NA2 = 2;
+  if (sm.total > p.smem_optin) {
+    sm = tc_smem(p, g->MT1, 1, t.O2G);
+    g->NA2 = 1;
+  }
+  g->a2_bytes = sm.a2_bytes;
+  g->off_xs = sm.off_xs;
+  g->off_a2 = sm.off_a2;
+  g->off_b2 = sm.off_b2;
+  g->off_a3 = sm.off_a3;
+  g->off_pbuf = sm.off_g1;
+  g->pbuf_stride = 0;
+  g->off_bar = sm.off_bar;
+  g->off_ys = 0;
+  const size_t slot_elems = (size_t)128 * t.O2G * c.O3;
+  // At least 120 KB, so no two CTAs share an SM: a CTA that holds TMEM and waits at the cluster
+  // barrier must never block a cluster peer inside tcgen05.alloc on the same SM.
+  g->smem = std::max<size_t>(sm.total, 120 * 1024);
+  if (g->smem > p.smem_optin) {
+    set_error("tcgen05 kernel needs %zu bytes of shared memory (device allows %zu)", g->smem,
+              p.smem_optin);
+    return TR_ERR_UNSUPPORTED;
+  }
+  const size_t counters = align_up((size_t)g->ntiles * t.NG * CL * sizeof(int), 256);
+  g->ws_bytes = 256 + counters +
+                (NC > 1 ? (size_t)g->ntiles * t.NG * NC * slot_elems * sizeof(float) : 0);
+  return TR_OK;
+}
+
 // Which kernel serves `T` tokens on this plan.
 static int pick_kind(const Plan& p, int64_t T, const tr_tiling* f) {
   if (f && f->kernel != KIND_AUTO) return f->kernel;
@@ -377,7 +521,12 @@ int tr_plan_create(const tr_spec* spec, int32_t dtype, int32_t device, tr_plan**
   }
   p->num_sms = nsm;
   p->smem_optin = (size_t)optin;
-  if (p->mma_ok) {
+  p->tc_ok = 0;
+  if (p->mma_ok) build_tc_layout(p);
+  if (p->tc_ok) {
+    p->packed_bytes =
+        align_up(p->t.off_b3 + (size_t)p->m.npieces * p->t.bytes_b3_piece, 256);
+  } else if (p->mma_ok) {
     p->packed_bytes = align_up(p->m.off_g3 + p->m.bytes_g3, 256);
   } else {
     p->packed_bytes = align_up(p->g.off_g3 + p->g.elems_g3 * elem_size(dtype), 256);
@@ -407,7 +556,7 @@ int tr_plan_flops_per_token(const tr_plan* plan, double* flops) {
 }
 
 static int geom_for(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling, int* kind,
-                    MmaGeom* g, DecodeGeom* dg) {
+                    MmaGeom* g, DecodeGeom* dg, TcGeom* tg) {
   if (!plan) {
     set_error("null plan");
     return TR_ERR_INVALID;
@@ -433,6 +582,12 @@ static int geom_for(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling
     if (tokens == 0) return TR_OK;
     return resolve_decode_geom(*plan, tokens, tiling, dg);
   }
+  if (*kind == KIND_TC05) {
+    memset(g, 0, sizeof(*g));
+    memset(tg, 0, sizeof(*tg));
+    if (tokens == 0) return TR_OK;
+    return resolve_tc_geom(*plan, tokens, tiling, tg);
+  }
   set_error("kernel kind %d not available in this build", *kind);
   return TR_ERR_UNSUPPORTED;
 }
@@ -446,9 +601,10 @@ int tr_workspace_bytes_tiled(const tr_plan* plan, int64_t tokens, const tr_tilin
   int kind;
   MmaGeom g;
   DecodeGeom dg;
-  const int st = geom_for(plan, tokens, tiling, &kind, &g, &dg);
+  TcGeom tg;
+  const int st = geom_for(plan, tokens, tiling, &kind, &g, &dg, &tg);
   if (st != TR_OK) return st;
-  *bytes = (kind == KIND_MMA) ? g.ws_bytes : 0;
+  *bytes = (kind == KIND_MMA) ? g.ws_bytes : (kind == KIND_TC05 ? tg.ws_bytes : 0);
   return TR_OK;
 }
 
@@ -478,9 +634,16 @@ int tr_plan_tiling(const tr_plan* plan, int64_t tokens, tr_tiling* out) {
   int kind;
   MmaGeom g;
   DecodeGeom dg;
-  const int st = geom_for(plan, tokens, nullptr, &kind, &g, &dg);
+  TcGeom tg;
+  const int st = geom_for(plan, tokens, nullptr, &kind, &g, &dg, &tg);
   if (st != TR_OK) return st;
   out->kernel = kind;
+  if (kind == KIND_TC05) {
+    out->tokens_per_tile = tg.TT;
+    out->cluster = tg.CL;
+    out->clusters = tg.NC;
+    return TR_OK;
+  }
   if (kind == KIND_DECODE) {
     out->tokens_per_tile = (int32_t)tokens;
     out->cluster = dg.CL;
@@ -499,7 +662,8 @@ int tr_forward_tiled(const tr_plan* plan, const void* packed, const void* x, int
   int kind;
   MmaGeom g;
   DecodeGeom dg;
-  int st = geom_for(plan, tokens, tiling, &kind, &g, &dg);
+  TcGeom tg;
+  int st = geom_for(plan, tokens, tiling, &kind, &g, &dg, &tg);
   if (st != TR_OK) return st;
   if (tokens == 0) return TR_OK;
   if (!packed || !x || !y) {
@@ -512,6 +676,18 @@ int tr_forward_tiled(const tr_plan* plan, const void* packed, const void* x, int
   }
   if (kind == KIND_GENERIC) return launch_generic(*plan, packed, x, tokens, y, stream);
   if (kind == KIND_DECODE) return launch_decode(*plan, dg, packed, x, tokens, y, stream);
+  if (kind == KIND_TC05) {
+    if (!workspace || workspace_bytes < tg.ws_bytes) {
+      set_error("workspace of %zu bytes needed, %zu given", tg.ws_bytes,
+                workspace ? workspace_bytes : (size_t)0);
+      return TR_ERR_WORKSPACE;
+    }
+    if ((uintptr_t)workspace & 15) {
+      set_error("workspace must be 16-byte aligned");
+      return TR_ERR_ALIGN;
+    }
+    return launch_tc05(*plan, tg, packed, x, tokens, y, workspace, stream);
+  }
   if (g.ws_bytes > 0) {
     if (!workspace || workspace_bytes < g.ws_bytes) {
       set_error("workspace of %zu bytes needed, %zu given", g.ws_bytes,

@@ -44,6 +44,22 @@ struct MmaLayout {
   size_t bytes_g1, bytes_g2, bytes_g3;
 };
 
+// Operand layout of the tcgen05 kernel (ring_tc05.cu): the UMMA B operands, K-major, no
+// swizzle, 8x8 core matrices (8 rows x 16 bytes) with LBO = 128 B between the K chunks of a row
+// group and SBO = K/8 * 128 B between row groups.
+//   B2 per o2 group g: rows (o2 of g, v padded to RP) = N2, K = K2P  (S2: G2[u,o2,i2,v])
+//   B3 per piece:      rows o3 padded to 16 = N3P, K = K3P (v padded to 16)  (S3: G3 slice)
+struct TcLayout {
+  int O2G;       // o2 modes per group (one CTA column of the grid)
+  int NG;        // groups
+  int N2;        // O2G * RP  (S2 N, D2 TMEM columns)
+  int N3P;       // O3 padded to 16 (S3 N per o2)
+  int K3P;       // RP padded to 16 (S3 K)
+  int tmem_cols; // power of two >= N2 + O2G * N3P
+  size_t off_b2, bytes_b2_group;
+  size_t off_b3, bytes_b3_piece;
+};
+
 // Canonical cores in natural [l][o][i][r] order (generic CUDA-core kernel, ring_generic.cu).
 struct GenericLayout {
   size_t off_g1, off_g2, off_g3;
@@ -59,7 +75,9 @@ struct Plan {
   Canon c;
   double macs_per_token;  // chosen order, multiply-adds per token
   int mma_ok;             // the mma.sync kernel handles this shape and dtype
+  int tc_ok;              // the tcgen05 kernel handles it (its operands are packed too)
   MmaLayout m;
+  TcLayout t;
   GenericLayout g;
   size_t packed_bytes;
   int num_sms;
@@ -99,6 +117,19 @@ struct DecodeGeom {
   size_t smem;
 };
 
+// Geometry of one tcgen05 launch: row tiles of TT tokens (M = 128 rows (t, o1)) x NG o2
+// groups x NJ = CL * NC CTAs splitting the pieces.
+struct TcGeom {
+  int TT, ntiles, MT1;
+  int CL, NC;
+  int NI3L;        // i3 values staged at once (1: streamed per i3)
+  int NA2;         // depth of the S2 A-operand ring (2 when it fits, else 1)
+  size_t a2_bytes;
+  size_t off_xs, off_a2, off_b2, off_a3, off_pbuf, pbuf_stride, off_bar, off_ys;
+  size_t smem;
+  size_t ws_bytes;
+};
+
 // Implemented in plan.cpp
 void set_error(const char* fmt, ...);
 int resolve_mma_geom(const Plan& p, int64_t T, const tr_tiling* force, MmaGeom* g);
@@ -114,6 +145,9 @@ int query_max_active_clusters(const Plan& p, const MmaGeom& g, int* n);
 int forward_noalloc(const Plan& p, const void* packed, const void* x, int64_t T, void* y,
                     void* stream);
 int resolve_decode_geom(const Plan& p, int64_t T, const tr_tiling* force, DecodeGeom* g);
+int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* force, TcGeom* g);
+int launch_tc05(const Plan& p, const TcGeom& g, const void* packed, const void* x, int64_t T,
+                void* y, void* ws, void* stream);
 int decode_variant(const Plan& p);
 int decode_max_threads(int variant);
 int launch_decode(const Plan& p, const DecodeGeom& g, const void* packed, const void* x,

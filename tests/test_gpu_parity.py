@@ -256,3 +256,43 @@ def test_generic_fp32_kernel_cross_checks_mma():
                                                                  for c in cores])
     check_close(y32, ref, torch.float32)
     check_close(y16, y32.double().cpu().numpy(), torch.float16)
+
+
+# tcgen05 kernel (forced; planner geometry or (tokens_per_tile, cluster, clusters)): ragged
+# row tiles, several o2 groups, DSMEM and workspace-slot reductions, one-piece CTAs
+TC_GEOMS = [(0, 0, 0), (0, 1, 1), (0, 4, 0), (0, 16, 1), (0, 2, 3), (5, 3, 2), (1, 8, 2)]
+
+
+@pytest.mark.parametrize("R", [8, 16])
+@pytest.mark.parametrize("geom", TC_GEOMS)
+def test_tcgen05_geometries(golden, R, geom):
+    key = f"req_r{R}"
+    fn = prepare_optimized(golden_cores(golden, key, torch.float16), kspec.TRSpec(rank=R))
+    TT, CL, NC = geom
+    for T in (8, 32):
+        if f"{key}_x_t{T}" not in golden:
+            continue
+        x = t(golden[f"{key}_x_t{T}"], torch.float16)
+        y1 = fn.call_tiled(x, abi.KERNEL_TC05, TT, CL, NC)
+        y2 = fn.call_tiled(x, abi.KERNEL_TC05, TT, CL, NC)
+        check_close(y1, golden[f"{key}_yref_t{T}"], torch.float16)
+        torch.testing.assert_close(y1, y2, rtol=0, atol=0)
+        assert fn.workspace[:4].view(torch.int32).item() == 0  # no bounded wait expired
+
+
+@pytest.mark.parametrize("name,T,dtype", [
+    ("odd", 9, torch.float16), ("odd16", 20, torch.float16), ("c5", 16, torch.bfloat16),
+    ("c4_q", 24, torch.bfloat16), ("c4_gate", 8, torch.bfloat16), ("c2", 200, torch.float16)])
+def test_tcgen05_shapes_against_oracle(name, T, dtype):
+    s = {"odd": kspec.TRSpec((2, 3, 4), (5, 6, 7), 3),
+         "odd16": kspec.TRSpec((8, 6, 20), (12, 5, 24), 16), "c5": kspec.SPEC_C5,
+         "c4_q": kspec.SPEC_C4["q"], "c4_gate": kspec.SPEC_C4["gate"], "c2": kspec.SPEC_C2}[name]
+    cores = kspec.baseline_cores(s, seed=3, dtype=dtype, device=DEV)
+    fn = prepare_optimized(cores, s)
+    x = kspec.baseline_x(s, T, seed=3, dtype=dtype, device=DEV)
+    y = fn.call_tiled(x, abi.KERNEL_TC05)
+    assert fn.workspace[:4].view(torch.int32).item() == 0
+    ref = oracle.tr_forward_reference(x.float().cpu().numpy(),
+                                      [c.float().cpu().numpy() for c in cores])
+    check_close(y, ref, dtype)
+    torch.testing.assert_close(fn.call_tiled(x, abi.KERNEL_TC05), y, rtol=0, atol=0)

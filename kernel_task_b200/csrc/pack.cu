@@ -128,22 +128,36 @@ __host__ __device__ inline size_t umma_kmajor_offset(int r, int k, int K) {
 }
 
 struct TcPackDims {
-  int I2, I3, O2, O3, R, RP, K2P, O2G, NG, N2, N3P, K3P, npieces;
+  int I1, I2, I3, O1, O2, O3, R, RP, K1P, N1P, K2P, O2G, NG, N2, N3P, K3P, npieces;
 };
 
-// tcgen05 B operands (fp16): B2 per o2 group [N2 rows (o2, v)] x [K2P (i2, u)] and B3 per piece
-// [N3P rows o3] x [K3P v]; zero where a padded index has no core entry.
+// tcgen05 B operands: B1 per s [N1P rows (o1, u)] x [K1P i1] in the input dtype E, B2 per o2
+// group [N2 rows (o2, v)] x [K2P (i2, u)] and B3 per piece [N3P rows o3] x [K3P v] in fp16; zero
+// where a padded index has no core entry.
 template <typename E>
-__global__ void pack_tc_kernel(CoreView<E> c1, CoreView<E> c2, TcPackDims d, unsigned char* b2,
-                               unsigned char* b3, size_t n2, size_t n3) {
-  const size_t total = n2 + n3;
+__global__ void pack_tc_kernel(CoreView<E> c0, CoreView<E> c1, CoreView<E> c2, TcPackDims d,
+                               unsigned char* b1, unsigned char* b2, unsigned char* b3, size_t n1,
+                               size_t n2, size_t n3) {
+  const size_t total = n1 + n2 + n3;
   for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
        idx += (size_t)gridDim.x * blockDim.x) {
+    if (idx < n1) {
+      const int k = (int)(idx % d.K1P);
+      size_t q = idx / d.K1P;
+      const int n = (int)(q % d.N1P);
+      const int s = (int)(q / d.N1P);
+      const int o1 = n / d.RP, u = n % d.RP;
+      const float v = (o1 < d.O1 && u < d.R && k < d.I1) ? c0.at(s, o1, k, u) : 0.f;
+      *reinterpret_cast<E*>(b1 + (size_t)s * d.N1P * d.K1P * sizeof(E) +
+                            umma_kmajor_offset(n, k, d.K1P)) = from_f32<E>(v);
+      continue;
+    }
     float v;
     unsigned char* dst;
-    if (idx < n2) {
-      const int k = (int)(idx % d.K2P);
-      size_t q = idx / d.K2P;
+    if (idx < n1 + n2) {
+      const size_t e = idx - n1;
+      const int k = (int)(e % d.K2P);
+      size_t q = e / d.K2P;
       const int n = (int)(q % d.N2);
       const int grp = (int)(q / d.N2);
       const int o2 = grp * d.O2G + n / d.RP, vv = n % d.RP;
@@ -151,7 +165,7 @@ __global__ void pack_tc_kernel(CoreView<E> c1, CoreView<E> c2, TcPackDims d, uns
       v = (o2 < d.O2 && vv < d.R && i2 < d.I2 && u < d.R) ? c1.at(u, o2, i2, vv) : 0.f;
       dst = b2 + (size_t)grp * d.N2 * d.K2P * 2 + umma_kmajor_offset(n, k, d.K2P);
     } else {
-      const size_t e = idx - n2;
+      const size_t e = idx - n1 - n2;
       const int k = (int)(e % d.K3P);
       size_t q = e / d.K3P;
       const int n = (int)(q % d.N3P);
@@ -193,14 +207,16 @@ static int pack_typed(const Plan& p, const void* const cores[3], void* packed, c
           n1, n2, n3);
       if (p.tc_ok) {
         const TcLayout& t = p.t;
-        TcPackDims td{c.I2, c.I3, c.O2, c.O3, c.R, m.RP, m.K2P, t.O2G, t.NG, t.N2, t.N3P, t.K3P,
-                      m.npieces};
+        TcPackDims td{c.I1, c.I2, c.I3, c.O1, c.O2, c.O3, c.R, m.RP, m.K1P, t.N1P, m.K2P, t.O2G,
+                      t.NG, t.N2, t.N3P, t.K3P, m.npieces};
+        const size_t tn1 = (size_t)c.R * t.N1P * m.K1P;
         const size_t tn2 = (size_t)t.NG * t.N2 * m.K2P;
         const size_t tn3 = (size_t)m.npieces * t.N3P * t.K3P;
-        const int tb = (int)std::min<size_t>((tn2 + tn3 + 255) / 256, 4096);
+        const int tb = (int)std::min<size_t>((tn1 + tn2 + tn3 + 255) / 256, 4096);
         pack_tc_kernel<E><<<tb, 256, 0, st>>>(
-            v[1], v[2], td, reinterpret_cast<unsigned char*>(base + t.off_b2),
-            reinterpret_cast<unsigned char*>(base + t.off_b3), tn2, tn3);
+            v[0], v[1], v[2], td, reinterpret_cast<unsigned char*>(base + t.off_b1),
+            reinterpret_cast<unsigned char*>(base + t.off_b2),
+            reinterpret_cast<unsigned char*>(base + t.off_b3), tn1, tn2, tn3);
       }
     }
   }

@@ -93,80 +93,115 @@ static void build_mma_layout(Plan* p) {
   m.off_g3 = align_up(m.off_g2 + m.bytes_g2, 256);
 }
 
-// Shared memory of one tcgen05 CTA (ring_tc05.cu):
-//   [x slice MT1*16 x (K1P+8)] [A2 x NA2] [G2 group] [A3 x 2] [G1 frags x 2] [G3 piece x 2]
-//   [mbarriers, TMEM slot, flags: 256 B]; the partial y (128 x O2G*O3 fp32) reuses offset 0.
+// Shared memory of one tcgen05 CTA (ring_tc05.cu), relative to a 1024-byte aligned base:
+//   A2 x NA2 (S2 A operand, 128-byte swizzle, 64-wide K slabs of 128 rows), B2 of the group,
+//   A3 x NA3 (S3 A operands of the group's o2), A1 x 2 (x slices), B1 x NB1, B3 x NB3,
+// reused after the piece loop as the CTA's fp32 partial y [128 rows x ystr], then the
+// mbarriers.  `total` includes 1 KB of slack for aligning the dynamic shared-memory window.
 struct TcSmem {
-  size_t off_xs, off_a2, a2_bytes, off_b2, off_a3, off_g1, off_bar, total;
+  size_t a2_bytes, a3_bytes, a1_bytes;
+  size_t off_a2, off_b2, off_a3, off_a1, off_g1, off_b3, off_bar, total;
 };
 
-static TcSmem tc_smem(const Plan& p, int MT1, int NA2, int O2G) {
+// Row stride of the partial y: at least O2G*O3 floats, 4 times an odd number (16-byte rows for
+// vector access, consecutive rows in different bank groups).
+static int tc_ystr(const Plan& p, int O2G) {
+  int w = (O2G * p.c.O3 + 3) / 4;
+  if ((w & 1) == 0) ++w;
+  return 4 * w;
+}
+
+static TcSmem tc_smem(const Plan& p, int O2G, int NA2, int NA3, int NB1, int NB3) {
   const MmaLayout& m = p.m;
   const TcLayout& t = p.t;
   TcSmem s;
-  const size_t xs = (size_t)MT1 * 16 * (m.KS1 * 16 + 8) * 2;
-  s.a2_bytes = (size_t)16 * (m.K2P / 8) * 144;
+  s.a2_bytes = (size_t)ceil_div(m.K2P, 64) * 128 * 128;
+  s.a3_bytes = (size_t)O2G * 128 * t.K3P * 2;
+  s.a1_bytes = (size_t)128 * m.K1P * 2;
+  const size_t b1 = (size_t)t.N1P * m.K1P * elem_size(p.dtype);
   const size_t b2 = (size_t)O2G * m.RP * m.K2P * 2;
-  const size_t a3 = (size_t)O2G * 128 * t.K3P * 2;
-  const size_t g1 = (size_t)m.KS1 * m.NT1 * 256;
   const size_t b3 = (size_t)t.N3P * t.K3P * 2;
-  s.off_xs = 0;
-  s.off_a2 = align_up(xs, 128);
-  s.off_b2 = align_up(s.off_a2 + NA2 * s.a2_bytes, 128);
+  s.off_a2 = 0;
+  s.off_b2 = s.off_a2 + NA2 * s.a2_bytes;
   s.off_a3 = align_up(s.off_b2 + b2, 128);
-  s.off_g1 = align_up(s.off_a3 + 2 * a3, 128);
-  const size_t main = s.off_g1 + 4 * g1 + 4 * b3;  // G1 and G3 rings of depth 4
-  const size_t ys = (size_t)128 * ((O2G * p.c.O3) | 1) * 4;
+  s.off_a1 = align_up(s.off_a3 + NA3 * s.a3_bytes, 128);
+  s.off_g1 = align_up(s.off_a1 + 2 * s.a1_bytes, 128);
+  s.off_b3 = align_up(s.off_g1 + NB1 * b1, 128);
+  const size_t main = s.off_b3 + NB3 * b3;
+  const size_t ys = (size_t)128 * tc_ystr(p, O2G) * 4;
   s.off_bar = align_up(std::max(main, ys), 128);
-  s.total = s.off_bar + 256;
+  s.total = s.off_bar + 512 + 1024;
   return s;
 }
 
 // tcgen05 operand layout (appended to the mma layout in the packed buffer).  O2 is split into
-// NG groups so that a CTA's TMEM holds two S2 accumulators (N2 columns each) and the S3
-// accumulators of its group (O2G x N3P columns) within 512 columns.
+// NG groups so that a CTA's TMEM holds its S1/S2 accumulators and the S3 accumulators of its
+// group (O2G x N3P columns) within 512 columns, and its operands fit in shared memory with
+// single buffers.  Of the TMEM arrangements the one giving the widest groups wins (fewer
+// groups: less repeated S1 work and fewer MMA instructions per call).  Needs RP <= 16 (one D1
+// row per TMEM lane and at most 256 S1 columns) and I2 <= 128.
 static void build_tc_layout(Plan* p) {
   const Canon& c = p->c;
   const MmaLayout& m = p->m;
   TcLayout& t = p->t;
+  p->tc_ok = 0;
+  if (m.RP > 16 || c.O1 > 128 || c.I2 > 128) return;
+  t.N1P = ceil_div(c.O1 * m.RP, 16) * 16;
   t.N3P = ceil_div(c.O3, 16) * 16;
   t.K3P = std::max(16, m.RP);
-  const int per_o2 = 2 * m.RP + t.N3P;
-  int o2g_max = std::min(512 / per_o2, 256 / m.RP);
-  if (o2g_max < 1) {
-    p->tc_ok = 0;
-    return;
-  }
-  t.NG = ceil_div(c.O2, o2g_max);
-  t.O2G = ceil_div(c.O2, t.NG);
-  if (m.RP == 8 && (t.O2G & 1)) t.O2G += 1;  // S2's N = O2G*8 must be a multiple of 16
-  t.NG = ceil_div(c.O2, t.O2G);
-  t.N2 = t.O2G * m.RP;
-  const int need = t.N2 * 2 + t.O2G * t.N3P;
-  t.tmem_cols = 32;
-  while (t.tmem_cols < need) t.tmem_cols *= 2;
-  // shrink the groups until the worst-case (TT = 128/O1) shared-memory footprint fits with a
-  // single A2 buffer (resolve_tc_geom takes two when they fit)
-  const int TTw = std::max(1, 128 / std::max(1, c.O1));
-  const int MT1w = ceil_div(TTw * c.I2, 16);
-  for (;;) {
-    if (tc_smem(*p, MT1w, 1, t.O2G).total <= p->smem_optin) break;
-    const int step = (m.RP == 8) ? 2 : 1;
-    if (t.O2G - step < 1) {
-      p->tc_ok = 0;
-      return;
+  if (t.N1P > 256 || t.N3P > 256) return;
+  const int step = (m.RP == 8) ? 2 : 1;  // S2's N = O2G * RP must be a multiple of 16
+  // arrangement: 0 separate ND1 = 2, 1 shared, 2 separate ND1 = 1 (order of preference on ties)
+  auto tmem_need = [&](int arr, int o2g) {
+    const int n2 = o2g * m.RP, d3 = o2g * t.N3P;
+    if (arr == 1) return 2 * std::max(t.N1P, n2) + d3;
+    return (arr == 0 ? 2 : 1) * t.N1P + 2 * n2 + d3;
+  };
+  auto largest_group = [&](int arr) {
+    int o2g = std::min(ceil_div(c.O2, step) * step, 256 / m.RP);
+    o2g -= o2g % step;
+    while (o2g >= step && tmem_need(arr, o2g) > 512) o2g -= step;
+    while (o2g >= step && tc_smem(*p, o2g, 1, 1, 2, 4).total > p->smem_optin) o2g -= step;
+    return o2g;
+  };
+  // balanced width of groups at most `o2g` wide: same group count, smallest width
+  auto balanced = [&](int o2g) {
+    int w = ceil_div(c.O2, ceil_div(c.O2, o2g));
+    if (w % step) w += step - w % step;
+    return std::min(w, o2g);
+  };
+  int best = -1, best_w = 0;
+  for (int arr = 0; arr < 3; ++arr) {
+    const int g = largest_group(arr);
+    if (g < step) continue;
+    if (balanced(g) > best_w) {
+      best_w = balanced(g);
+      best = arr;
     }
-    t.O2G -= step;
   }
+  if (best < 0) return;
+  t.O2G = best_w;
   t.NG = ceil_div(c.O2, t.O2G);
   t.N2 = t.O2G * m.RP;
+  t.shared_d12 = best == 1;
+  t.ND1 = best == 0 ? 2 : 1;
+  t.DBW = std::max(t.N1P, t.N2);
+  if (t.shared_d12) {
+    t.d2_col = 0;
+    t.d3_col = 2 * t.DBW;
+  } else {
+    t.d2_col = t.ND1 * t.N1P;
+    t.d3_col = t.d2_col + 2 * t.N2;
+  }
   t.tmem_cols = 32;
-  while (t.tmem_cols < t.N2 * 2 + t.O2G * t.N3P) t.tmem_cols *= 2;
+  while (t.tmem_cols < tmem_need(best, t.O2G)) t.tmem_cols *= 2;
+  t.bytes_b1_slice = (size_t)t.N1P * m.K1P * elem_size(p->dtype);
   t.bytes_b2_group = (size_t)t.N2 * m.K2P * 2;
   t.bytes_b3_piece = (size_t)t.N3P * t.K3P * 2;
-  t.off_b2 = align_up(m.off_g3 + m.bytes_g3, 256);
+  t.off_b1 = align_up(m.off_g3 + m.bytes_g3, 256);
+  t.off_b2 = align_up(t.off_b1 + (size_t)c.R * t.bytes_b1_slice, 256);
   t.off_b3 = align_up(t.off_b2 + (size_t)t.NG * t.bytes_b2_group, 256);
-  p->tc_ok = p->mma_ok && c.O1 <= 128 && t.tmem_cols <= 512 && t.N3P <= 256;
+  p->tc_ok = p->mma_ok && t.tmem_cols <= 512;
 }
 
 static void build_generic_layout(Plan* p) {
@@ -255,7 +290,7 @@ int resolve_mma_geom(const Plan& p, int64_t T, const tr_tiling* f, MmaGeom* g) {
     CL = f->cluster;
     NC = f->clusters > 0 ? f->clusters : 1;
   } else {
-    int NJ = g->ntiles >= p.num_sms ? 1 : std::max(1, p.num_sms / g->ntiles);
+    int NJ = g->ntiles >= p.num_sms ? 1 : std::max(1, p.num_sms / std::max(1, g->ntiles));
     NJ = std::min(NJ, m.npieces);
     CL = std::min(8, NJ);
     NC = std::max(1, NJ / CL);
@@ -361,25 +396,27 @@ int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* f, TcGeom* g) {
     set_error("tcgen05 kernel does not support this spec/dtype");
     return TR_ERR_UNSUPPORTED;
   }
-  int TT = (f && f->tokens_per_tile > 0) ? f->tokens_per_tile : std::max(1, 128 / c.O1);
+  // a row tile: TT tokens, TT*O1 rows (t, o1) of S2/S3 and TT*I2 rows (t, i2) of S1, each <= 128
+  const int tt_max = std::max(1, std::min(128 / c.O1, 128 / c.I2));
+  int TT = (f && f->tokens_per_tile > 0) ? f->tokens_per_tile : tt_max;
   if (TT > T) TT = (int)T;
   if (TT < 1) TT = 1;
-  if (TT * c.O1 > 128) {
-    set_error("tokens_per_tile=%d x O1=%d exceeds the 128-row tile", TT, c.O1);
+  if (TT > tt_max) {
+    set_error("tokens_per_tile=%d exceeds the 128-row tile (at most %d tokens: O1=%d, I2=%d)",
+              TT, tt_max, c.O1, c.I2);
     return TR_ERR_INVALID;
   }
   g->TT = TT;
   g->ntiles = (int)((T + TT - 1) / TT);
-  g->MT1 = ceil_div(TT * c.I2, 16);
   int CL, NC;
   if (f && f->cluster > 0) {
     CL = f->cluster;
     NC = f->clusters > 0 ? f->clusters : 1;
   } else {
-    const long long cols = (long long)g->ntiles * t.NG;
+    const long long cols = std::max<long long>(1, (long long)g->ntiles * t.NG);
     int NJ = cols >= p.num_sms ? 1 : (int)std::max<long long>(1, p.num_sms / cols);
     NJ = std::min(NJ, m.npieces);
-    CL = std::min(8, NJ);
+    CL = std::min(16, NJ);
     NC = std::max(1, NJ / CL);
   }
   if (CL < 1 || CL > 16 || NC < 1 || (long long)CL * NC > m.npieces) {
@@ -388,31 +425,55 @@ int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* f, TcGeom* g) {
   }
   g->CL = CL;
   g->NC = NC;
-  g->NI3L = 1;
-  TcSmem sm = tc_smem(p, g->MT1, 2, t.O2G);
-  g->NA2 = 2;
-  if (sm.total > p.smem_optin) {
-    sm = tc_smem(p, g->MT1, 1, t.O2G);
-    g->NA2 = 1;
+  // buffer depths, deepest first: A2, A3 double; B1 all R slices, else a ring; B3 the CTA's
+  // whole piece range (at most 64 pieces), else a ring of 4
+  const int NJ = CL * NC;
+  const int max_np = (m.npieces + NJ - 1) / NJ;
+  TcSmem sm{};
+  bool fits = false;
+  for (int na2 = 2; na2 >= 1 && !fits; --na2) {
+    for (int na3 = 2; na3 >= 1 && !fits; --na3) {
+      const int b1_opts[4] = {c.R, 4, 3, 2};
+      for (int i1 = 0; i1 < 4 && !fits; ++i1) {
+        const int nb1 = b1_opts[i1];
+        if (i1 > 0 && nb1 >= c.R) continue;
+        for (int i3 = 0; i3 < 2 && !fits; ++i3) {
+          const int nb3 = i3 == 0 ? max_np : 4;
+          if (i3 == 0 && max_np > 64) continue;
+          sm = tc_smem(p, t.O2G, na2, na3, nb1, nb3);
+          if (sm.total <= p.smem_optin) {
+            fits = true;
+            g->NA2 = na2;
+            g->NA3 = na3;
+            g->NB1 = nb1;
+            g->b1_all = nb1 >= c.R;
+            g->NB3 = nb3;
+            g->b3_all = i3 == 0;
+          }
+        }
+      }
+    }
   }
+  if (!fits) {
+    set_error("tcgen05 kernel needs %zu bytes of shared memory (device allows %zu)", sm.total,
+              p.smem_optin);
+    return TR_ERR_UNSUPPORTED;
+  }
+  g->ystr = tc_ystr(p, t.O2G);
   g->a2_bytes = sm.a2_bytes;
-  g->off_xs = sm.off_xs;
+  g->a3_bytes = sm.a3_bytes;
+  g->a1_bytes = sm.a1_bytes;
   g->off_a2 = sm.off_a2;
   g->off_b2 = sm.off_b2;
   g->off_a3 = sm.off_a3;
-  g->off_pbuf = sm.off_g1;
-  g->pbuf_stride = 0;
+  g->off_a1 = sm.off_a1;
+  g->off_g1 = sm.off_g1;
+  g->off_b3 = sm.off_b3;
   g->off_bar = sm.off_bar;
-  g->off_ys = 0;
   const size_t slot_elems = (size_t)128 * t.O2G * c.O3;
   // At least 120 KB, so no two CTAs share an SM: a CTA that holds TMEM and waits at the cluster
   // barrier must never block a cluster peer inside tcgen05.alloc on the same SM.
   g->smem = std::max<size_t>(sm.total, 120 * 1024);
-  if (g->smem > p.smem_optin) {
-    set_error("tcgen05 kernel needs %zu bytes of shared memory (device allows %zu)", g->smem,
-              p.smem_optin);
-    return TR_ERR_UNSUPPORTED;
-  }
   const size_t counters = align_up((size_t)g->ntiles * t.NG * CL * sizeof(int), 256);
   g->ws_bytes = 256 + counters +
                 (NC > 1 ? (size_t)g->ntiles * t.NG * NC * slot_elems * sizeof(float) : 0);
@@ -426,6 +487,8 @@ static int pick_kind(const Plan& p, int64_t T, const tr_tiling* f) {
     DecodeGeom d;
     if (T >= 1 && T * p.c.O1 <= 16 && resolve_decode_geom(p, T, nullptr, &d) == TR_OK)
       return KIND_DECODE;
+    TcGeom tg;
+    if (T >= 1 && p.tc_ok && resolve_tc_geom(p, T, nullptr, &tg) == TR_OK) return KIND_TC05;
     return KIND_MMA;
   }
   return KIND_GENERIC;
@@ -758,10 +821,13 @@ int tr_plan_describe(const tr_plan* plan, char* buf, size_t len) {
       "{\"order\": \"%c%c%c\", \"reversed\": %d, \"canonical_in\": [%d, %d, %d], "
       "\"canonical_out\": [%d, %d, %d], \"rank\": %d, \"macs_per_token\": %.0f, "
       "\"mma\": %d, \"rank_padded\": %d, \"pieces\": %d, \"packed_bytes\": %zu, "
-      "\"dtype\": %d}",
+      "\"dtype\": %d, \"tcgen05\": %d, \"o2_group\": %d, \"groups\": %d, "
+      "\"tmem_cols\": %d, \"d1_buffers\": %d, \"shared_d12\": %d}",
       names[c.role[0]], names[c.role[1]], names[c.role[2]], c.reversed, c.I1, c.I2, c.I3, c.O1,
       c.O2, c.O3, c.R, plan->macs_per_token, plan->mma_ok, m.RP, m.npieces, plan->packed_bytes,
-      plan->dtype);
+      plan->dtype, plan->tc_ok, plan->tc_ok ? plan->t.O2G : 0, plan->tc_ok ? plan->t.NG : 0,
+      plan->tc_ok ? plan->t.tmem_cols : 0, plan->tc_ok ? plan->t.ND1 : 0,
+      plan->tc_ok ? plan->t.shared_d12 : 0);
   if (n < 0 || (size_t)n >= len) {
     set_error("buffer too small");
     return TR_ERR_INVALID;

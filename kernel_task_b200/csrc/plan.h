@@ -47,15 +47,26 @@ struct MmaLayout {
 // Operand layout of the tcgen05 kernel (ring_tc05.cu): the UMMA B operands, K-major, no
 // swizzle, 8x8 core matrices (8 rows x 16 bytes) with LBO = 128 B between the K chunks of a row
 // group and SBO = K/8 * 128 B between row groups.
-//   B2 per o2 group g: rows (o2 of g, v padded to RP) = N2, K = K2P  (S2: G2[u,o2,i2,v])
-//   B3 per piece:      rows o3 padded to 16 = N3P, K = K3P (v padded to 16)  (S3: G3 slice)
+//   B1 per s:          rows (o1, u padded to RP) = N1P, K = K1P (i1)  (S1: G1[s,o1,i1,u], dtype E)
+//   B2 per o2 group g: rows (o2 of g, v padded to RP) = N2, K = K2P  (S2: G2[u,o2,i2,v], fp16)
+//   B3 per piece:      rows o3 padded to 16 = N3P, K = K3P (v padded to 16)  (S3: G3 slice, fp16)
+// TMEM columns of a CTA, in one of two arrangements:
+//   separate: D1 x ND1 [0, ND1 N1P), D2 x 2 [d2_col, d2_col + 2 N2), D3 [d3_col, + O2G N3P)
+//   shared:   two buffers of DBW = max(N1P, N2) columns, each holding a piece's D1 and then, once
+//             the converters have read it, the same piece's D2; D3 [d3_col, + O2G N3P)
 struct TcLayout {
   int O2G;       // o2 modes per group (one CTA column of the grid)
   int NG;        // groups
+  int shared_d12;  // 1: D1 and D2 share the two buffers
+  int ND1;       // separate arrangement: S1 accumulators (1 or 2)
+  int DBW;       // shared arrangement: buffer width
+  int N1P;       // O1 * RP padded to 16 (S1 N, D1 TMEM columns)
   int N2;        // O2G * RP  (S2 N, D2 TMEM columns)
   int N3P;       // O3 padded to 16 (S3 N per o2)
   int K3P;       // RP padded to 16 (S3 K)
-  int tmem_cols; // power of two >= N2 + O2G * N3P
+  int d2_col, d3_col;
+  int tmem_cols; // power of two >= N1P + 2 N2 + O2G N3P
+  size_t off_b1, bytes_b1_slice;
   size_t off_b2, bytes_b2_group;
   size_t off_b3, bytes_b3_piece;
 };
@@ -120,12 +131,14 @@ struct DecodeGeom {
 // Geometry of one tcgen05 launch: row tiles of TT tokens (M = 128 rows (t, o1)) x NG o2
 // groups x NJ = CL * NC CTAs splitting the pieces.
 struct TcGeom {
-  int TT, ntiles, MT1;
+  int TT, ntiles;
   int CL, NC;
-  int NI3L;        // i3 values staged at once (1: streamed per i3)
-  int NA2;         // depth of the S2 A-operand ring (2 when it fits, else 1)
-  size_t a2_bytes;
-  size_t off_xs, off_a2, off_b2, off_a3, off_pbuf, pbuf_stride, off_bar, off_ys;
+  int NA2, NA3;        // depths of the A2 and A3 operand buffers
+  int NB1, b1_all;     // B1 slots; b1_all: all R slices loaded once, else a ring of NB1
+  int NB3, b3_all;     // B3 slots; b3_all: the CTA's whole piece range loaded once, else a ring
+  int ystr;            // row stride (floats) of the partial y in shared memory
+  size_t a2_bytes, a3_bytes, a1_bytes;
+  size_t off_a2, off_b2, off_a3, off_a1, off_g1, off_b3, off_bar;
   size_t smem;
   size_t ws_bytes;
 };

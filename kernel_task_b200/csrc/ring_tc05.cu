@@ -1,31 +1,47 @@
 // Fused tensor-ring kernel on the 5th-generation tensor cores (tcgen05, TMEM accumulators) for
-// token counts with several 128-row tiles of S2 rows (t, o1).  One launch per call.
+// token counts that fill 128-row tiles.  One launch per call; every contraction of the ring runs
+// as tcgen05.mma with operands in shared memory and accumulators in TMEM.
 //
-// Per CTA: one row tile (TT tokens -> M = 128 rows (t, o1), zero-padded), one group of O2G output
-// modes o2, and a contiguous range of ring pieces (i3, s).  Warp-specialised pipeline over the
-// pieces, each stage handing buffers to the next through mbarriers:
-//   warps 4-11  S1 (mma.sync): T1[(t,o1),(i2,u)] = sum_i1 x[t,i1,i2,i3] G1[s,o1,i1,u], written
-//               straight into the K-major UMMA layout of S2's A operand (A2 ring, NA2 deep)
-//   warp 12     issues every tcgen05.mma from one thread:
-//               S2  D2[b] (TMEM, 2 buffers) = A2 . G2[(i2,u), (o2 of group, v)]
-//               S3  D3[o2] (TMEM, accumulated over all pieces) += A3[b][o2] . G3_piece
-//               and the TMA bulk copies of G2 (once) and the per-piece G3 operand (2-deep ring)
-//   warps 0-3   read D2[b] from TMEM (one row per thread), round to fp16, write A3[b]
-// G1 fragments of each piece arrive by TMA bulk copy (2-deep ring) issued by the S1 warps.
-// After the last piece D3 is read out, summed across the cluster's CTAs through distributed
-// shared memory (and across clusters through workspace slots when NC > 1) and written as y.
+// Per CTA: one row tile of TT tokens, one group of O2G output modes o2, and a contiguous range of
+// ring pieces (i3, s).  Per piece:
+//   S1  D1[(t,i2), (o1,u)]  = A1[(t,i2), i1] . B1_s[(o1,u), i1]        A1 = x slice of this i3
+//   C1  D1 -> A2[(t,o1), (i2,u)] (fp16): the transpose between S1's rows and S2's rows goes
+//       TMEM -> registers -> shared memory, one D1 row (t,i2) per thread
+//   S2  D2[(t,o1), (o2,v)]  = A2 . B2[(o2 of group, v), (i2,u)]
+//   C2  D2 -> A3[o2][(t,o1), v] (fp16)
+//   S3  D3[o2][(t,o1), o3] += A3[o2] . B3_piece[o3, v]                  (accumulated over pieces)
+// D1 and D2 live either in separate TMEM buffers (one or two D1, two D2) or, when that makes the
+// o2 groups wider, in two shared buffers that hold a piece's D1 and then its D2.
+// Roles (448 threads):
+//   warps 0-7   C1 (warps w and w+4 read the same TMEM lanes, each half of the o1 range); after
+//               each piece one C1 thread issues S2 of that piece and, with separate TMEM
+//               buffers, S1 of a later piece into the D1 buffer just read
+//   warps 8-11  C2; after each piece one C2 thread issues S3 of that piece and, with shared
+//               buffers, S1 of the piece two later into the buffer just read; then the D3
+//               read-out with warps 0-7
+//   warp 12     TMA loader: B2 once; B1 and B3 all at once when they fit, else rings refilled
+//               as the tensor-core stages release their slots
+//   warp 13     stages the x slice A1 of each further i3 (the first two are staged by everyone)
+// Each converter group synchronises on a named barrier before its thread issues, so a stage's
+// MMAs start as soon as their operands are written; the tensor-core stages signal their
+// consumers with one tcgen05.commit each (S1DONE, S2DONE, S3DONE).  After the last piece D3 is
+// summed across the cluster's CTAs through distributed shared memory (and across clusters
+// through workspace slots when NC > 1) and written as y.
 //
-// Shared-memory operands use the no-swizzle K-major canonical layout: 8 x 16-byte core matrices,
-// LBO between the K chunks of a row group, SBO between row groups.  A2 uses LBO = 144 B so that
-// the S1 fragment stores of one warp (eight K chunks of one row group) hit distinct banks.
+// Shared-memory operand layouts (K-major):
+//   A2  128-byte swizzle: 64-element K slabs of 128 rows x 128 B, row groups 1024 B apart, the
+//       16-byte chunk index XOR (row & 7); C1 rotates each lane's chunk order so that the eight
+//       lanes of a store phase hit eight different bank groups
+//   A1, B1, B2, A3, B3  no swizzle: 8 rows x 16 B core matrices, LBO 128 B, SBO = K/8 * 128 B
 //
 // Every wait on an mbarrier is bounded; on expiry the CTA raises a shared abort flag (all later
-// waits return at once), records TR_ERR_TIMEOUT in the status word, still releases its TMEM and
-// returns.
+// waits return at once), records TR_ERR_TIMEOUT in the status word, waits (bounded) for its own
+// bulk copies and tensor-core work in flight, releases its TMEM and returns.
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "device_util.cuh"
 #include "plan.h"
@@ -35,24 +51,26 @@ namespace cg = cooperative_groups;
 
 namespace trr {
 
-constexpr int kTcThreads = 416;  // 4 converter warps + 8 S1 warps + 1 MMA warp
-constexpr int kS1Threads = 256;
-constexpr int kA2Lbo = 144;
-constexpr unsigned kWaitLimit = 1u << 24;
-// mbarrier slots
-constexpr int kRing = 4;  // depth of the per-piece G1 and G3 operand rings
+constexpr int kTcThreads = 448;
+constexpr int kBuildThreads = 416;  // every warp but the loader: first x slices
+constexpr unsigned kWaitLimit = 1u << 16;   // try_wait rounds before a wait gives up
+constexpr unsigned kSuspendNs = 20000;       // suspend-time hint of one try_wait round
+constexpr unsigned kPollLimit = 1u << 24;    // loader polls without progress before it gives up
+constexpr int kA2Slab = 128 * 128;  // bytes of one 64-wide K slab of A2
+
 enum {
-  BAR_A2FULL = 0,   // [2] S1 -> MMA (count 8: one arrive per S1 warp)
-  BAR_A2FREE = 2,   // [2] MMA commit after S2 -> S1
-  BAR_D2FULL = 4,   // [2] MMA commit after S2 -> converters
-  BAR_D2FREE = 6,   // [2] converters (count 4) -> MMA
-  BAR_A3FULL = 8,   // [2] converters (count 4) -> MMA
-  BAR_A3FREE = 10,  // [2] MMA commit after S3 -> converters, G3 ring refill
-  BAR_B3FULL = 12,  // [kRing] G3 bulk copy landed
-  BAR_G1FULL = 16,  // [kRing] G1 bulk copy landed
-  BAR_B2FULL = 20,  // G2 bulk copy landed
-  BAR_D3DONE = 21,  // last S3 complete
-  BAR_COUNT = 22
+  BAR_A1FULL = 0,   // [2] x slice staged (count 1)
+  BAR_A1FREE = 2,   // [2] commit after the last S1 of that i3
+  BAR_G1FULL = 4,   // [4] B1 landed (slot 0 only when all slices load at once)
+  BAR_S1DONE = 8,   // [4] commit after S1(j), index j % 4
+  BAR_S2DONE = 12,  // [2] commit after S2(j), index j % 2
+  BAR_D2FREE = 14,  // [2] separate TMEM arrangement: C2 warps read D2 (count 4)
+  BAR_S3DONE = 16,  // [4] commit after S3(j), index j % 4
+  BAR_B3FULL = 20,  // [4] B3 landed (slot 0 only when the whole range loads at once)
+  BAR_B2FULL = 24,  // B2 landed
+  BAR_D3DONE = 25,  // commit after the last S3: every tensor-core operation completed
+  BAR_DRAIN = 26,   // [2] after a timeout: the two issuing threads' own work completed
+  BAR_COUNT = 28
 };
 
 template <class S>
@@ -60,42 +78,44 @@ struct TcParams {
   S sh;
   const void* x;
   void* y;
-  const uint2* g1f;
+  const unsigned char* b1;
   const unsigned char* b2;
   const unsigned char* b3;
   float* slots;
   int* cnt;
   int* status;
-  int T;
-  int TT, MT1, CL, NC, NG, O2G, N2, N3P, K3P, tmem_cols;
-  int g1p_bytes, b2_bytes, b3p_bytes;
-  int off_xs, off_a2, off_b2, off_a3, off_g1, off_b3, off_bar;
-  int NA2, a2_bytes, a3_bytes;
-  int a2_sbo, slot_elems;
+  int T, TT, CL, NC, NG, O2G;
+  int shared_d12, ND1, DBW, N1P, N2, N3P, d2_col, d3_col, tmem_cols;
+  int b1_bytes, b2_bytes, b3_bytes;
+  int off_a2, off_b2, off_a3, off_a1, off_g1, off_b3, off_bar;
+  int NA2, NA3, NB1, b1_all, NB3, b3_all, a2_bytes, a3_bytes, a1_bytes;
+  int ystr, vec_out, slot_elems;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
 
-// UMMA shared-memory matrix descriptor: no swizzle, K-major, sm_100 version field = 1.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
-  d |= (uint64_t)1 << 46;
-  return d;
+// UMMA shared-memory matrix descriptors (sm_100 version field = 1).
+__device__ __forceinline__ uint64_t desc_plain(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | (uint64_t)((lbo >> 4) & 0x3FFFu) << 16 |
+         (uint64_t)((sbo >> 4) & 0x3FFFu) << 32 | (uint64_t)1 << 46;
+}
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | (uint64_t)1 << 16 | (uint64_t)(1024 >> 4) << 32 |
+         (uint64_t)1 << 46 | (uint64_t)2 << 61;
 }
 
-// kind::f16 instruction descriptor: fp16 A and B, fp32 D, both K-major, M x N.
-__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N) {
-  return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) |
-         ((uint32_t)(M >> 4) << 24);
+// kind::f16 instruction descriptor: A and B both of type E (fp16 or bf16), fp32 D, K-major.
+template <typename E>
+__host__ __device__ constexpr uint32_t umma_idesc(int M, int N) {
+  return (1u << 4) | ((std::is_same<E, __nv_bfloat16>::value ? 1u : 0u) << 7) |
+         ((std::is_same<E, __nv_bfloat16>::value ? 1u : 0u) << 10) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t dtmem, uint64_t da, uint64_t db, uint32_t idesc,
-                                         uint32_t accumulate) {
+__device__ __forceinline__ void umma(uint32_t dtmem, uint64_t da, uint64_t db, uint32_t idesc,
+                                     uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(
@@ -119,26 +139,47 @@ __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
 }
 
-// Bounded wait for the mbarrier phase with parity `parity` to complete: a non-blocking
-// test_wait spin (a suspended try_wait wakes up late enough to dominate a short pipeline stage).
-// Gives up at once when the CTA's abort flag is set, and sets it when the bound runs out.
+__device__ __forceinline__ bool mbar_test(uint32_t mbar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(mbar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// One try_wait round: the thread may be suspended until the phase completes or about
+// kSuspendNs pass, without spinning on the barrier.
+__device__ __forceinline__ bool mbar_try(uint32_t mbar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(done)
+      : "r"(mbar), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait for the phase with parity `parity` to complete.  Gives up at once when the CTA's
+// abort flag is set, and sets it when the bound runs out.
 __device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, volatile int* abort) {
+  if (mbar_test(mbar, parity)) return true;  // already complete: a test costs a few cycles
   for (unsigned i = 0; i < kWaitLimit; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(done)
-        : "r"(mbar), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if ((i & 255) == 255) {
-      if (*abort) return false;
-      __nanosleep(32);
-    }
+    if (mbar_try(mbar, parity)) return true;
+    if (*abort) return false;
   }
   *abort = 1;
   return false;
+}
+
+// Bounded wait that ignores the abort flag: draining the CTA's own work in flight.
+__device__ __forceinline__ void mbar_drain(uint32_t mbar, uint32_t parity) {
+  if (mbar_test(mbar, parity)) return;
+  for (unsigned i = 0; i < kWaitLimit && !mbar_try(mbar, parity); ++i) {
+  }
 }
 
 __device__ __forceinline__ void mbar_arrive(uint32_t mbar) {
@@ -157,12 +198,22 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       : "memory");
 }
 
-__device__ __forceinline__ void s1_bar_sync() {
-  asm volatile("bar.sync 1, %0;\n" ::"n"(kS1Threads) : "memory");
+// Named barrier `id` over the first `n` threads that reach it (a multiple of 32).
+__device__ __forceinline__ void named_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]);
+template <>
+__device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
       "%14,%15}, [%16];\n"
@@ -170,29 +221,65 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
         "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
 
-__device__ __forceinline__ void copy_async16(unsigned char* dst, const void* src, int bytes,
-                                             int tid, int nthr) {
-  const uint32_t s = smem_u32(dst);
-  const char* g = static_cast<const char*>(src);
-  for (int i = tid * 16; i < bytes; i += nthr * 16)
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s + i), "l"(g + i)
-                 : "memory");
+// Eight fp32 (as raw TMEM words) -> one 16-byte chunk of fp16.
+__device__ __forceinline__ uint4 chunk_f16(const uint32_t* w) {
+  uint4 q;
+  q.x = pack2<__half>(__uint_as_float(w[0]), __uint_as_float(w[1]));
+  q.y = pack2<__half>(__uint_as_float(w[2]), __uint_as_float(w[3]));
+  q.z = pack2<__half>(__uint_as_float(w[4]), __uint_as_float(w[5]));
+  q.w = pack2<__half>(__uint_as_float(w[6]), __uint_as_float(w[7]));
+  return q;
+}
+
+// Byte offset of 16-byte chunk kc (K elements 8 kc .. 8 kc + 7) of row `row` in A2.
+__device__ __forceinline__ uint32_t a2_offset(int row, int kc) {
+  return (uint32_t)((kc >> 3) * kA2Slab + (row >> 3) * 1024 + (row & 7) * 128 +
+                    (((kc & 7) ^ (row & 7)) << 4));
+}
+
+// Stage the x slice of one i3 as S1's A operand: rows (t, i2) of the tile (zero beyond TTv
+// tokens), K = i1 padded to K1P.  Thread `bt` of `nb` builds 16-byte chunks bt, bt + nb, ...
+template <class S>
+__device__ __forceinline__ void build_a1(const S& sh, unsigned char* a1,
+                                         const unsigned short* xt, int TTv, int i3, int bt,
+                                         int nb) {
+  const int kch = sh.KS1 * 2;
+  const int nchunks = 128 * kch;
+  const uint32_t sbo = (uint32_t)kch * 128;
+  for (int e = bt; e < nchunks; e += nb) {
+    const int r = e / kch, kc = e - r * kch;
+    const int t = r / sh.I2, i2 = r - t * sh.I2;
+    unsigned short v[8];
+    const unsigned short* row = xt + (size_t)t * sh.d_in + i2 * sh.sx2 + i3 * sh.sx3;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i1 = kc * 8 + k;
+      v[k] = (t < TTv && i1 < sh.I1) ? __ldg(row + i1 * sh.sx1) : (unsigned short)0;
+    }
+    uint4 q;
+    q.x = v[0] | (uint32_t)v[1] << 16;
+    q.y = v[2] | (uint32_t)v[3] << 16;
+    q.z = v[4] | (uint32_t)v[5] << 16;
+    q.w = v[6] | (uint32_t)v[7] << 16;
+    *reinterpret_cast<uint4*>(a1 + (r >> 3) * sbo + kc * 128 + (r & 7) * 16) = q;
+  }
 }
 
 template <class S, typename E, int RP>
 __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams<S> p) {
+  static_assert(RP == 8 || RP == 16, "tcgen05 kernel: rank padded to 8 or 16");
   const S& sh = p.sh;
-  constexpr int K3 = RP < 16 ? 16 : RP;   // S3 K (v padded to 16)
-  extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int K3 = 16;         // S3 K (v padded to 16)
+  constexpr int NCH = RP / 8;    // 16-byte chunks of one (o1 or o2, i2) run of RP values
+  constexpr int OB = 64 / RP;    // o1 per TMEM batch in C1 (64 columns)
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, t4 = lane & 3;
   cg::cluster_group cluster = cg::this_cluster();
 
   const int NJ = p.CL * p.NC;
@@ -205,6 +292,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   const int pa = (int)((long long)bj * sh.npieces / NJ);
   const int pb = (int)((long long)(bj + 1) * sh.npieces / NJ);
   const int np = pb - pa;
+  const int i3a = pa / sh.R;
+  const int nq = np > 0 ? (pb - 1) / sh.R - i3a + 1 : 0;  // i3 values of the range
   const int t0 = tile * p.TT;
   const int TTv = min(p.TT, p.T - t0);
   const int rows = TTv * sh.O1;
@@ -217,8 +306,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   int* flag = reinterpret_cast<int*>(smem + p.off_bar + BAR_COUNT * 8 + 4);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + p.off_bar + BAR_COUNT * 8 + 8);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  const unsigned short* xt = static_cast<const unsigned short*>(p.x) + (size_t)t0 * sh.d_in;
+  // TMEM columns of piece j's S1 and S2 accumulators
+  auto d1_col = [&](int j) { return p.shared_d12 ? (j & 1) * p.DBW : (j % p.ND1) * p.N1P; };
+  auto d2_col = [&](int j) { return p.shared_d12 ? (j & 1) * p.DBW : p.d2_col + (j & 1) * p.N2; };
 
-  // ---- TMEM, mbarriers, zeroed operand buffers (padded rows and K columns contribute nothing)
+  // ---- TMEM, mbarriers, zeroed pads of the A operands (never-written rows/columns)
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
                      smem_u32(tmem_slot)),
@@ -226,23 +319,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
   }
-  if (tid == 0) {
-    const int counts[BAR_COUNT] = {8, 8, 1, 1, 1, 1, 4, 4, 4, 4, 1, 1,
-                                   1, 1, 1, 1, 1, 1, 1, 1, 1, 1};
-    for (int i = 0; i < BAR_COUNT; ++i)
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar(i)), "r"(counts[i])
+  if (tid == 32) {
+    for (int i = 0; i < BAR_COUNT; ++i) {
+      const int count = (i >= BAR_D2FREE && i < BAR_S3DONE) ? 4 : 1;
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar(i)), "r"(count)
                    : "memory");
+    }
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     *flag = 0;
     *abort = 0;
   }
-  {
+  if (p.TT * sh.O1 < 128 || sh.I2 * RP < sh.K2P) {
     uint4* z = reinterpret_cast<uint4*>(smem + p.off_a2);
     const int n16 = p.NA2 * p.a2_bytes / 16;
     for (int i = tid; i < n16; i += kTcThreads) z[i] = make_uint4(0u, 0u, 0u, 0u);
-    uint4* z3 = reinterpret_cast<uint4*>(smem + p.off_a3);
-    const int n3 = 2 * p.a3_bytes / 16;
-    for (int i = tid; i < n3; i += kTcThreads) z3[i] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  if (RP < K3) {
+    uint4* z = reinterpret_cast<uint4*>(smem + p.off_a3);
+    const int n16 = p.NA3 * p.a3_bytes / 16;
+    for (int i = tid; i < n16; i += kTcThreads) z[i] = make_uint4(0u, 0u, 0u, 0u);
   }
   fence_async_smem();
   tc_fence_before();
@@ -251,235 +346,292 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   const uint32_t tmem = *tmem_slot;
   const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
 
+  const uint32_t a1s = smem_u32(smem + p.off_a1);
+  const uint32_t g1s = smem_u32(smem + p.off_g1);
+  const uint32_t a2s = smem_u32(smem + p.off_a2);
+  const uint32_t b2s = smem_u32(smem + p.off_b2);
+  const uint32_t a3s = smem_u32(smem + p.off_a3);
+  const uint32_t b3s = smem_u32(smem + p.off_b3);
+  const int NB1 = p.NB1;
+
+  // S1(k) from one thread: waits for its x slice and B1, accumulates into D1(k), signals
+  // S1DONE (and A1FREE after the last piece of an i3).  False when a wait gave up.
+  auto issue_s1 = [&](int k) -> bool {
+    const int q = (pa + k) / sh.R - i3a;
+    bool ok = mbar_wait(bar(BAR_A1FULL + (q & 1)), (q >> 1) & 1, abort);
+    if (ok)
+      ok = p.b1_all ? mbar_wait(bar(BAR_G1FULL), 0, abort)
+                    : mbar_wait(bar(BAR_G1FULL + k % NB1), (k / NB1) & 1, abort);
+    if (!ok) return false;
+    tc_fence_after();
+    const uint32_t a1 = a1s + (q & 1) * p.a1_bytes;
+    const uint32_t b1 = g1s + (p.b1_all ? (pa + k) % sh.R : k % NB1) * p.b1_bytes;
+    const uint32_t sbo1 = (uint32_t)sh.KS1 * 256;
+    const uint32_t idesc1 = umma_idesc<E>(128, p.N1P);
+    for (int ks = 0; ks < sh.KS1; ++ks)
+      umma(tmem + d1_col(k), desc_plain(a1 + ks * 256, 128, sbo1),
+           desc_plain(b1 + ks * 256, 128, sbo1), idesc1, ks > 0 ? 1u : 0u);
+    umma_commit(bar(BAR_S1DONE + (k & 3)));
+    if (k == np - 1 || (pa + k + 1) % sh.R == 0) umma_commit(bar(BAR_A1FREE + (q & 1)));
+    return true;
+  };
+
   if (warp == 12) {
-    // ================================ MMA issuer ================================
+    // ============================ TMA loader ============================
     if (lane == 0 && np > 0) {
-      const uint32_t b2s = smem_u32(smem + p.off_b2);
-      const uint32_t idesc2 = umma_idesc_f16(128, p.N2);
-      const uint32_t idesc3 = umma_idesc_f16(128, p.N3P);
-      const int b2_sbo = (sh.K2P / 8) * 128;
-      const int b3_sbo = (K3 / 8) * 128;
       bulk_load(b2s, p.b2 + (size_t)grp * p.b2_bytes, p.b2_bytes, bar(BAR_B2FULL));
-      for (int q = 0; q < kRing && q < np; ++q)
-        bulk_load(smem_u32(smem + p.off_b3 + q * p.b3p_bytes),
-                  p.b3 + (size_t)(pa + q) * p.b3p_bytes, p.b3p_bytes, bar(BAR_B3FULL + q));
-      bool ok = mbar_wait(bar(BAR_B2FULL), 0, abort);
-      for (int j = 0; j <= np && ok; ++j) {
-        if (j < np) {  // ---- S2(j)
-          const int ab = j % p.NA2, db = j & 1;
-          ok = mbar_wait(bar(BAR_A2FULL + ab), (uint32_t)((j / p.NA2) & 1), abort);
-          if (ok && j >= 2) ok = mbar_wait(bar(BAR_D2FREE + db), (uint32_t)(((j >> 1) - 1) & 1), abort);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t a2s = smem_u32(smem + p.off_a2 + ab * p.a2_bytes);
-          for (int ks = 0; ks < sh.KS2; ++ks) {
-            const uint64_t da = umma_desc(a2s + ks * 2 * kA2Lbo, kA2Lbo, p.a2_sbo);
-            const uint64_t db2 = umma_desc(b2s + ks * 2 * 128, 128, b2_sbo);
-            umma_f16(tmem + db * p.N2, da, db2, idesc2, ks > 0 ? 1u : 0u);
-          }
-          umma_commit(bar(BAR_A2FREE + ab));
-          umma_commit(bar(BAR_D2FULL + db));
+      if (p.b1_all) {
+        bulk_load(g1s, p.b1, sh.R * p.b1_bytes, bar(BAR_G1FULL));
+      } else {
+        for (int q = 0; q < NB1 && q < np; ++q)
+          bulk_load(g1s + q * p.b1_bytes, p.b1 + (size_t)((pa + q) % sh.R) * p.b1_bytes,
+                    p.b1_bytes, bar(BAR_G1FULL + q));
+      }
+      if (p.b3_all) {
+        bulk_load(b3s, p.b3 + (size_t)pa * p.b3_bytes, np * p.b3_bytes, bar(BAR_B3FULL));
+      } else {
+        for (int q = 0; q < 4 && q < np; ++q)
+          bulk_load(b3s + q * p.b3_bytes, p.b3 + (size_t)(pa + q) * p.b3_bytes, p.b3_bytes,
+                    bar(BAR_B3FULL + q));
+      }
+      // rings: refill a slot once the S1 / S3 of the piece NB1 / 4 earlier has completed
+      int r1 = p.b1_all ? np : min(NB1, np), r3 = p.b3_all ? np : min(4, np);
+      unsigned idle = 0;
+      while ((r1 < np || r3 < np) && !*abort) {
+        bool prog = false;
+        if (r1 < np && mbar_test(bar(BAR_S1DONE + ((r1 - NB1) & 3)), ((r1 - NB1) >> 2) & 1)) {
+          bulk_load(g1s + (r1 % NB1) * p.b1_bytes, p.b1 + (size_t)((pa + r1) % sh.R) * p.b1_bytes,
+                    p.b1_bytes, bar(BAR_G1FULL + r1 % NB1));
+          ++r1;
+          prog = true;
         }
-        if (j >= 1) {  // ---- S3(j-1)
-          const int jj = j - 1, bb = jj & 1, rb = jj % kRing;
-          // Refill the G3 slot of piece jj-2 with piece jj+2.  S3(jj-2) completes phase
-          // (jj-2)/2 of A3FREE[bb]; wait for it before S3(jj) is committed to the same barrier,
-          // so the phase being waited for cannot have been overtaken by the next one.
-          if (jj >= 2 && jj + 2 < np) {
-            const int old = jj - 2;
-            ok = mbar_wait(bar(BAR_A3FREE + bb), (uint32_t)((old >> 1) & 1), abort);
-            if (!ok) break;
-            const int slot = (jj + 2) % kRing;
-            bulk_load(smem_u32(smem + p.off_b3 + slot * p.b3p_bytes),
-                      p.b3 + (size_t)(pa + jj + 2) * p.b3p_bytes, p.b3p_bytes,
-                      bar(BAR_B3FULL + slot));
-          }
-          ok = mbar_wait(bar(BAR_A3FULL + bb), (uint32_t)((jj >> 1) & 1), abort);
-          if (ok) ok = mbar_wait(bar(BAR_B3FULL + rb), (uint32_t)((jj / kRing) & 1), abort);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t a3s = smem_u32(smem + p.off_a3 + bb * p.a3_bytes);
-          const uint32_t b3s = smem_u32(smem + p.off_b3 + rb * p.b3p_bytes);
-          for (int o = 0; o < o2n; ++o) {
-#pragma unroll
-            for (int ks = 0; ks < K3 / 16; ++ks) {
-              const uint64_t da = umma_desc(a3s + o * a3_block + ks * 256, 128, (K3 / 8) * 128);
-              const uint64_t db3 = umma_desc(b3s + ks * 256, 128, b3_sbo);
-              umma_f16(tmem + 2 * p.N2 + o * p.N3P, da, db3, idesc3,
-                       (jj > 0 || ks > 0) ? 1u : 0u);
-            }
-          }
-          umma_commit(bar(BAR_A3FREE + bb));
+        if (r3 < np && mbar_test(bar(BAR_S3DONE + ((r3 - 4) & 3)), ((r3 - 4) >> 2) & 1)) {
+          bulk_load(b3s + (r3 & 3) * p.b3_bytes, p.b3 + (size_t)(pa + r3) * p.b3_bytes, p.b3_bytes,
+                    bar(BAR_B3FULL + (r3 & 3)));
+          ++r3;
+          prog = true;
+        }
+        if (prog) {
+          idle = 0;
+        } else if (++idle >= kPollLimit) {
+          *abort = 1;
+        } else {
+          __nanosleep(64);
         }
       }
-      umma_commit(bar(BAR_D3DONE));
+      if (*abort) {  // drain this CTA's bulk copies before leaving
+        mbar_drain(bar(BAR_B2FULL), 0);
+        if (p.b1_all) mbar_drain(bar(BAR_G1FULL), 0);
+        else
+          for (int q = max(0, r1 - NB1); q < r1; ++q)
+            mbar_drain(bar(BAR_G1FULL + q % NB1), (q / NB1) & 1);
+        if (p.b3_all) mbar_drain(bar(BAR_B3FULL), 0);
+        else
+          for (int q = max(0, r3 - 4); q < r3; ++q) mbar_drain(bar(BAR_B3FULL + (q & 3)), (q >> 2) & 1);
+      }
     }
     __syncwarp();
-  } else if (warp >= 4) {
-    // ================================ S1 producers ================================
-    const int sw = warp - 4, st = tid - 128;
-    const int XSTR = (sh.KS1 * 16) + 8;
-    const int M1P = p.MT1 * 16;
-    const int s1rows = TTv * sh.I2;
-    const int njobs1 = p.MT1 * sh.NT1;
-    E* xs = reinterpret_cast<E*>(smem + p.off_xs);
-    const E* x = static_cast<const E*>(p.x) + (size_t)t0 * sh.d_in;
-    if (st == 0)
-      for (int q = 0; q < kRing && q < np; ++q)
-        bulk_load(smem_u32(smem + p.off_g1 + q * p.g1p_bytes),
-                  p.g1f + (size_t)((pa + q) % sh.R) * sh.KS1 * sh.NT1 * 32, p.g1p_bytes,
-                  bar(BAR_G1FULL + q));
-    int cur_i3 = -1;
-    bool ok = true;
-    for (int j = 0; j < np; ++j) {
-      const int pi = pa + j, i3 = pi / sh.R;
-      if (i3 != cur_i3) {  // x slice of this i3: rows (t, i2), columns i1 (zero padded)
-        s1_bar_sync();
-        const int n = M1P * XSTR;
-        for (int e = st; e < n; e += kS1Threads) {
-          const int r = e / XSTR, c = e - r * XSTR;
-          E v = from_f32<E>(0.f);
-          if (r < s1rows && c < sh.I1) {
-            const int t = r / sh.I2, i2 = r - t * sh.I2;
-            v = x[(size_t)t * sh.d_in + c * sh.sx1 + i2 * sh.sx2 + i3 * sh.sx3];
-          }
-          xs[e] = v;
-        }
-        s1_bar_sync();
-        cur_i3 = i3;
+  } else {
+    // ---- first x slices, staged by every thread but the loader's
+    const int bt = tid < 384 ? tid : tid - 32;
+    for (int q = 0; q < 2 && q < nq; ++q)
+      build_a1(sh, smem + p.off_a1 + q * p.a1_bytes, xt, TTv, i3a + q, bt, kBuildThreads);
+    fence_async_smem();
+    named_sync(1, kBuildThreads);
+    if (tid == 0)
+      for (int q = 0; q < 2 && q < nq; ++q) mbar_arrive(bar(BAR_A1FULL + q));
+
+    if (warp < 8) {
+      // ============================ C1: D1 -> A2, issues S2 (and S1) ============================
+      const int r1 = 32 * (warp & 3) + lane;  // D1 row (t, i2)
+      const int tq = r1 / sh.I2, i2 = r1 - tq * sh.I2;
+      const bool rvalid = tq < p.TT;
+      const int h = (sh.O1 + 1) >> 1;
+      const int o1a = (warp >> 2) ? h : 0, o1b = (warp >> 2) ? sh.O1 : h;
+      const int rot = NCH == 2 ? ((i2 >> 2) & 1) : 0;
+      bool ok = true, b2ok = false;
+      if (tid == 0) {  // the first S1s: as many as there are D1 buffers
+        const int first = p.shared_d12 ? 2 : p.ND1;
+        for (int k = 0; k < first && k < np && ok; ++k) ok = issue_s1(k);
       }
-      const int gb = j % kRing, ab = j % p.NA2;
-      if (ok) ok = mbar_wait(bar(BAR_G1FULL + gb), (uint32_t)((j / kRing) & 1), abort);
-      if (ok && j >= p.NA2)
-        ok = mbar_wait(bar(BAR_A2FREE + ab), (uint32_t)(((j / p.NA2) - 1) & 1), abort);
-      if (ok) {
-        unsigned char* a2 = smem + p.off_a2 + ab * p.a2_bytes;
-        const uint2* g1p = reinterpret_cast<const uint2*>(smem + p.off_g1 + gb * p.g1p_bytes) + lane;
-        // four independent jobs at a time: (m16 tile, n8 tile) = job / NT1, job % NT1
-        for (int jb = sw; jb < njobs1; jb += 4 * (kS1Threads / 32)) {
-          float d[4][4];
-          int jobs[4];
+      for (int j = 0; j < np; ++j) {
+        const int ab = j % p.NA2;
+        if (ok) ok = mbar_wait(bar(BAR_S1DONE + (j & 3)), (j >> 2) & 1, abort);
+        if (ok && j >= p.NA2)  // S2 of the piece that last used this A2 buffer completed
+          ok = mbar_wait(bar(BAR_S2DONE + ((j - p.NA2) & 1)), ((j - p.NA2) >> 1) & 1, abort);
+        tc_fence_after();
+        if (ok) {
+          unsigned char* a2 = smem + p.off_a2 + ab * p.a2_bytes;
+          const uint32_t d1 = tmem + lane_base + d1_col(j);
+          for (int ob = o1a; ob < o1b; ob += OB) {
+            uint32_t v[OB][RP];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            jobs[u] = jb + u * (kS1Threads / 32);
+            for (int u = 0; u < OB; ++u)
+              if (ob + u < o1b) tmem_ld<RP>(d1 + (ob + u) * RP, v[u]);
+            tmem_wait_ld();
+            if (rvalid) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) d[u][c] = 0.f;
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if (jobs[u] < njobs1) {
-              const int mt1 = jobs[u] / sh.NT1, nt1 = jobs[u] - mt1 * sh.NT1;
-              for (int ks = 0; ks < sh.KS1; ++ks) {
-                uint32_t a[4];
-                ldsm_x4(a, xs + (size_t)(mt1 * 16 + (lane & 15)) * XSTR + ks * 16 +
-                               (lane >> 4) * 8);
-                const uint2 b = g1p[(size_t)(ks * sh.NT1 + nt1) * 32];
-                mma_16816(d[u], a, b.x, b.y, E());
-              }
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if (jobs[u] < njobs1) {
-              const int mt1 = jobs[u] / sh.NT1, nt1 = jobs[u] - mt1 * sh.NT1;
-              const int col = nt1 * 8 + 2 * t4;
-              const int o1 = col / RP, uu = col % RP;
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int r = mt1 * 16 + g + 8 * h;
-                if (r < s1rows) {
-                  const int t = r / sh.I2, i2 = r - t * sh.I2;
-                  const int row = t * sh.O1 + o1, k = i2 * RP + uu;
-                  *reinterpret_cast<__half2*>(a2 + (row >> 3) * p.a2_sbo + (k >> 3) * kA2Lbo +
-                                              (row & 7) * 16 + (k & 7) * 2) =
-                      __floats2half2_rn(d[u][2 * h], d[u][2 * h + 1]);
+              for (int u = 0; u < OB; ++u) {
+                if (ob + u < o1b) {
+                  const int row = tq * sh.O1 + ob + u;
+                  if (NCH == 1) {
+                    *reinterpret_cast<uint4*>(a2 + a2_offset(row, i2)) = chunk_f16(v[u]);
+                  } else {
+                    const uint4 c0 = chunk_f16(v[u]), c1 = chunk_f16(v[u] + 8);
+                    *reinterpret_cast<uint4*>(a2 + a2_offset(row, 2 * i2 + rot)) = rot ? c1 : c0;
+                    *reinterpret_cast<uint4*>(a2 + a2_offset(row, 2 * i2 + (rot ^ 1))) =
+                        rot ? c0 : c1;
+                  }
                 }
               }
             }
           }
+          fence_async_smem();
         }
-        fence_async_smem();
+        tc_fence_before();
+        named_sync(2, 256);  // all of D1(j) read, all of A2(j) written
+        if (tid == 0 && ok && !*abort) {
+          tc_fence_after();
+          // ---- S2(j): D2 buffer drained by C2 (separate arrangement), B2 landed
+          if (!b2ok) ok = b2ok = mbar_wait(bar(BAR_B2FULL), 0, abort);
+          if (ok && !p.shared_d12 && j >= 2)
+            ok = mbar_wait(bar(BAR_D2FREE + (j & 1)), ((j >> 1) - 1) & 1, abort);
+          if (ok) {
+            tc_fence_after();
+            const uint32_t a2 = a2s + ab * p.a2_bytes;
+            const uint32_t sbo2 = (uint32_t)(sh.K2P / 8) * 128;
+            const uint32_t idesc2 = umma_idesc<__half>(128, p.N2);
+            for (int ks = 0; ks < sh.KS2; ++ks)
+              umma(tmem + d2_col(j), desc_sw128(a2 + (ks >> 2) * kA2Slab + (ks & 3) * 32),
+                   desc_plain(b2s + ks * 256, 128, sbo2), idesc2, ks > 0 ? 1u : 0u);
+            umma_commit(bar(BAR_S2DONE + (j & 1)));
+          }
+          // ---- S1(j + ND1) into the D1 buffer just read (separate arrangement)
+          if (ok && !p.shared_d12 && j + p.ND1 < np) ok = issue_s1(j + p.ND1);
+        }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(BAR_A2FULL + ab));
-      s1_bar_sync();  // every S1 warp is done with G1 slot gb
-      if (st == 0 && ok && j + kRing < np)
-        bulk_load(smem_u32(smem + p.off_g1 + gb * p.g1p_bytes),
-                  p.g1f + (size_t)((pa + j + kRing) % sh.R) * sh.KS1 * sh.NT1 * 32, p.g1p_bytes,
-                  bar(BAR_G1FULL + gb));
-    }
-  } else {
-    // ================================ D2 -> A3 converters ================================
-    const int r = 32 * warp + lane;
-    bool ok = true;
-    for (int j = 0; j < np; ++j) {
-      const int db = j & 1, ab = j & 1;
-      if (ok) ok = mbar_wait(bar(BAR_D2FULL + db), (uint32_t)((j >> 1) & 1), abort);
-      if (ok && j >= 2) ok = mbar_wait(bar(BAR_A3FREE + ab), (uint32_t)(((j >> 1) - 1) & 1), abort);
-      tc_fence_after();
-      if (ok) {
-        const uint32_t d2 = tmem + db * p.N2 + lane_base;
-        unsigned char* rowp = smem + p.off_a3 + ab * p.a3_bytes + (r >> 3) * ((K3 / 8) * 128) +
-                              (r & 7) * 16;
-        // 64 columns per batch: issue every TMEM load of the batch, then wait once
-        for (int c0 = 0; c0 < p.N2; c0 += 64) {
-          float v[4][16];
+      if (tid == 0 && *abort) {  // drain this thread's tensor-core work
+        umma_commit(bar(BAR_DRAIN));
+        mbar_drain(bar(BAR_DRAIN), 0);
+      }
+    } else if (warp < 12) {
+      // ============================ C2: D2 -> A3, issues S3 (and S1) ============================
+      const int r = 32 * (warp & 3) + lane;  // row (t, o1)
+      bool ok = true;
+      for (int j = 0; j < np; ++j) {
+        const int db = j & 1, ab = j % p.NA3;
+        if (ok) ok = mbar_wait(bar(BAR_S2DONE + db), (j >> 1) & 1, abort);
+        if (ok && j >= p.NA3)  // S3 of the piece that last used this A3 buffer completed
+          ok = mbar_wait(bar(BAR_S3DONE + ((j - p.NA3) & 3)), ((j - p.NA3) >> 2) & 1, abort);
+        tc_fence_after();
+        if (ok) {
+          const uint32_t d2 = tmem + lane_base + d2_col(j);
+          unsigned char* rowp =
+              smem + p.off_a3 + ab * p.a3_bytes + (r >> 3) * ((K3 / 8) * 128) + (r & 7) * 16;
+          for (int c0 = 0; c0 < p.N2; c0 += 64) {
+            uint32_t v[4][16];
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            if (c0 + c * 16 < p.N2) tmem_ld16(d2 + c0 + c * 16, v[c]);
-          tmem_wait_ld();
+            for (int c = 0; c < 4; ++c)
+              if (c0 + c * 16 < p.N2) tmem_ld<16>(d2 + c0 + c * 16, v[c]);
+            tmem_wait_ld();
+            if (!p.shared_d12 && c0 + 64 >= p.N2) {  // last read of D2: C1 may reuse the buffer
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(bar(BAR_D2FREE + db));
+            }
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 4; ++c) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int col = c0 + c * 16 + 8 * h;  // D2 column = o * RP + v
-              if (col < p.N2) {
-                const int o = col / RP, vv = col % RP;
-                uint4 q;
-                q.x = pack2<__half>(v[c][8 * h + 0], v[c][8 * h + 1]);
-                q.y = pack2<__half>(v[c][8 * h + 2], v[c][8 * h + 3]);
-                q.z = pack2<__half>(v[c][8 * h + 4], v[c][8 * h + 5]);
-                q.w = pack2<__half>(v[c][8 * h + 6], v[c][8 * h + 7]);
-                *reinterpret_cast<uint4*>(rowp + o * a3_block + (vv >> 3) * 128) = q;
+              for (int hh = 0; hh < 2; ++hh) {
+                const int col = c0 + c * 16 + 8 * hh;  // D2 column = o * RP + v
+                if (col < p.N2) {
+                  const int o = col / RP, vv = col % RP;
+                  *reinterpret_cast<uint4*>(rowp + o * a3_block + (vv >> 3) * 128) =
+                      chunk_f16(v[c] + 8 * hh);
+                }
               }
             }
           }
+          fence_async_smem();
+        } else if (!p.shared_d12) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(BAR_D2FREE + db));
         }
-        fence_async_smem();
+        tc_fence_before();
+        named_sync(3, 128);  // all of D2(j) read, all of A3(j) written
+        if (tid == 256 && ok && !*abort) {
+          tc_fence_after();
+          // ---- S3(j): B3 landed
+          ok = p.b3_all ? mbar_wait(bar(BAR_B3FULL), 0, abort)
+                        : mbar_wait(bar(BAR_B3FULL + (j & 3)), (j >> 2) & 1, abort);
+          if (ok) {
+            tc_fence_after();
+            const uint32_t a3 = a3s + ab * p.a3_bytes;
+            const uint32_t b3 = b3s + (p.b3_all ? j : (j & 3)) * p.b3_bytes;
+            const uint32_t sbo3 = (uint32_t)(K3 / 8) * 128;
+            const uint32_t idesc3 = umma_idesc<__half>(128, p.N3P);
+            for (int o = 0; o < o2n; ++o)
+              umma(tmem + p.d3_col + o * p.N3P, desc_plain(a3 + o * a3_block, 128, sbo3),
+                   desc_plain(b3, 128, sbo3), idesc3, j > 0 ? 1u : 0u);
+            umma_commit(bar(BAR_S3DONE + (j & 3)));
+            if (j == np - 1) umma_commit(bar(BAR_D3DONE));
+          }
+          // ---- S1(j + 2) into the buffer that held D2(j) (shared arrangement)
+          if (ok && p.shared_d12 && j + 2 < np) ok = issue_s1(j + 2);
+        }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(bar(BAR_D2FREE + db));
-        mbar_arrive(bar(BAR_A3FULL + ab));
+      if (tid == 256 && *abort) {  // drain this thread's tensor-core work
+        umma_commit(bar(BAR_DRAIN + 1));
+        mbar_drain(bar(BAR_DRAIN + 1), 0);
+      }
+    } else {
+      // ============================ x slices of further i3 ============================
+      bool ok = true;
+      for (int q = 2; q < nq; ++q) {
+        if (ok) ok = mbar_wait(bar(BAR_A1FREE + (q & 1)), ((q >> 1) - 1) & 1, abort);
+        if (ok) {
+          build_a1(sh, smem + p.off_a1 + (q & 1) * p.a1_bytes, xt, TTv, i3a + q, lane, 32);
+          fence_async_smem();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(BAR_A1FULL + (q & 1)));
       }
     }
   }
 
   // ---- D3 -> partial y of this CTA (rows (t,o1), columns (o of group, o3)), fp32 in smem.
-  // Every role is past its last use of the operand space; D3DONE means every MMA completed.
+  // D3DONE: every tensor-core operation completed, so the operand space is free.
   __syncthreads();
   float* ys = reinterpret_cast<float*>(smem);
-  const int ystr = (p.O2G * sh.O3) | 1;  // odd row stride: one bank per row of the warp
-  if (warp < 4) {
+  const int ystr = p.ystr;
+  if (warp < 12) {
     const bool ok = np > 0 && mbar_wait(bar(BAR_D3DONE), 0, abort);
     tc_fence_after();
-    const int r = 32 * warp + lane;
-    for (int o = 0; o < o2n; ++o) {
+    const int r = 32 * (warp & 3) + lane;
+    const bool vec4 = (sh.O3 & 3) == 0;
+    for (int o = warp >> 2; o < o2n; o += 3) {
       for (int c16 = 0; c16 < p.N3P / 16; ++c16) {
-        float v[16];
+        uint32_t v[16];
         if (ok) {
-          tmem_ld16(tmem + 2 * p.N2 + lane_base + o * p.N3P + c16 * 16, v);
+          tmem_ld<16>(tmem + lane_base + p.d3_col + o * p.N3P + c16 * 16, v);
           tmem_wait_ld();
         } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = 0.f;
+          for (int i = 0; i < 16; ++i) v[i] = 0u;
         }
         if (r < rows) {
+          float* dst = ys + r * ystr + o * sh.O3 + c16 * 16;
+          if (vec4) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int o3 = c16 * 16 + i;
-            if (o3 < sh.O3) ys[r * ystr + o * sh.O3 + o3] = v[i];
+            for (int k = 0; k < 4; ++k)
+              if (c16 * 16 + 4 * k < sh.O3)
+                *reinterpret_cast<float4*>(dst + 4 * k) =
+                    make_float4(__uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
+                                __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3]));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (c16 * 16 + i < sh.O3) dst[i] = __uint_as_float(v[i]);
           }
         }
       }
@@ -497,56 +649,116 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
 
   // ---- reduce over the cluster: each CTA sums its slice of the tile from every peer's partial
   // (distributed shared memory, rank order), then across clusters through workspace slots
-  const int nout = rows * o2n * sh.O3;
-  const int SL = (nout + p.CL - 1) / p.CL;
   if (p.CL > 1) cluster.sync();  // all peers' partials are in their shared memory
-  const float* peer[16];
-#pragma unroll
-  for (int k = 0; k < 16; ++k) peer[k] = (p.CL > 1 && k < p.CL) ? cluster.map_shared_rank(ys, k) : ys;
+  auto peer = [&](int k) -> const float* { return p.CL > 1 ? cluster.map_shared_rank(ys, k) : ys; };
   E* y = static_cast<E*>(p.y) + (size_t)t0 * sh.d_out;
-  const int ebeg = crank * SL;
-  const int eend = min(nout, ebeg + SL);
   float* slot = p.NC > 1
       ? p.slots + (((size_t)tile * p.NG + grp) * p.NC + cl_id) * (size_t)p.slot_elems
       : nullptr;
-  for (int e = ebeg + tid; e < eend; e += kTcThreads) {
-    const int o3 = e % sh.O3, q = e / sh.O3;
-    const int o = q % o2n, r = q / o2n;
-    const int idx = r * ystr + o * sh.O3 + o3;
-    float v[16];
-#pragma unroll
-    for (int k = 0; k < 16; ++k) v[k] = k < p.CL ? peer[k][idx] : 0.f;
-    float sum = 0.f;
-#pragma unroll
-    for (int k = 0; k < 16; ++k) sum += v[k];
-    if (p.NC > 1) {
-      slot[e] = sum;
-    } else {
-      const int t = r / sh.O1, o1 = r - t * sh.O1;
-      y[(size_t)t * sh.d_out + o1 * sh.sy1 + (o2a + o) * sh.sy2 + o3 * sh.sy3] =
-          from_f32<E>(sum);
+  const float* s0 = p.slots + ((size_t)tile * p.NG + grp) * p.NC * (size_t)p.slot_elems;
+  if (p.vec_out) {
+    // 8 consecutive o3 per item: two float4 per partial, one 16-byte store of y
+    const int nv3 = sh.O3 / 8;
+    const int nout = rows * o2n * nv3;
+    const int SL = (nout + p.CL - 1) / p.CL;
+    const int ebeg = crank * SL, eend = min(nout, ebeg + SL);
+    for (int e = ebeg + tid; e < eend; e += kTcThreads) {
+      const int o3v = e % nv3, q = e / nv3;
+      const int o = q % o2n, r = q / o2n;
+      const int idx = r * ystr + o * sh.O3 + o3v * 8;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+      for (int k = 0; k < p.CL; ++k) {
+        const float* pk = peer(k);
+        const float4 u = *reinterpret_cast<const float4*>(pk + idx);
+        const float4 w = *reinterpret_cast<const float4*>(pk + idx + 4);
+        a.x += u.x; a.y += u.y; a.z += u.z; a.w += u.w;
+        b.x += w.x; b.y += w.y; b.z += w.z; b.w += w.w;
+      }
+      if (p.NC > 1) {
+        float4* d = reinterpret_cast<float4*>(slot + (size_t)(r * o2n + o) * sh.O3 + o3v * 8);
+        d[0] = a;
+        d[1] = b;
+      } else {
+        const int t = r / sh.O1, o1 = r - t * sh.O1;
+        uint4 out;
+        out.x = pack2<E>(a.x, a.y);
+        out.y = pack2<E>(a.z, a.w);
+        out.z = pack2<E>(b.x, b.y);
+        out.w = pack2<E>(b.z, b.w);
+        *reinterpret_cast<uint4*>(y + (size_t)t * sh.d_out + o1 * sh.sy1 + (o2a + o) * sh.sy2 +
+                                  o3v * 8) = out;
+      }
     }
-  }
-  if (p.CL > 1) cluster.sync();  // peers finished reading this CTA's shared memory
-  if (p.NC > 1) {
-    __threadfence();
-    __syncthreads();
-    int* counter = p.cnt + ((size_t)tile * p.NG + grp) * p.CL + crank;
-    if (tid == 0) *flag = (atomicAdd(counter, 1) == p.NC - 1);
-    __syncthreads();
-    if (*flag) {  // last cluster for this slice: add the NC slots in cluster order, write y
+    if (p.CL > 1) cluster.sync();  // peers finished reading this CTA's shared memory
+    if (p.NC > 1) {
       __threadfence();
-      const float* s0 = p.slots + ((size_t)tile * p.NG + grp) * p.NC * (size_t)p.slot_elems;
-      for (int e = ebeg + tid; e < eend; e += kTcThreads) {
-        float sum = 0.f;
-        for (int c = 0; c < p.NC; ++c) sum += __ldcg(s0 + (size_t)c * p.slot_elems + e);
-        const int o3 = e % sh.O3, q = e / sh.O3;
-        const int o = q % o2n, r = q / o2n;
+      __syncthreads();
+      int* counter = p.cnt + ((size_t)tile * p.NG + grp) * p.CL + crank;
+      if (tid == 0) *flag = (atomicAdd(counter, 1) == p.NC - 1);
+      __syncthreads();
+      if (*flag) {  // last cluster for this slice: add the NC slots in cluster order, write y
+        __threadfence();
+        for (int e = ebeg + tid; e < eend; e += kTcThreads) {
+          const int o3v = e % nv3, q = e / nv3;
+          const int o = q % o2n, r = q / o2n;
+          const size_t off = (size_t)(r * o2n + o) * sh.O3 + o3v * 8;
+          float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+          for (int c = 0; c < p.NC; ++c) {
+            const float4 u = __ldcg(reinterpret_cast<const float4*>(s0 + (size_t)c * p.slot_elems + off));
+            const float4 w = __ldcg(reinterpret_cast<const float4*>(s0 + (size_t)c * p.slot_elems + off + 4));
+            a.x += u.x; a.y += u.y; a.z += u.z; a.w += u.w;
+            b.x += w.x; b.y += w.y; b.z += w.z; b.w += w.w;
+          }
+          const int t = r / sh.O1, o1 = r - t * sh.O1;
+          uint4 out;
+          out.x = pack2<E>(a.x, a.y);
+          out.y = pack2<E>(a.z, a.w);
+          out.z = pack2<E>(b.x, b.y);
+          out.w = pack2<E>(b.z, b.w);
+          *reinterpret_cast<uint4*>(y + (size_t)t * sh.d_out + o1 * sh.sy1 + (o2a + o) * sh.sy2 +
+                                    o3v * 8) = out;
+        }
+        if (tid == 0) atomicExch(counter, 0);
+      }
+    }
+  } else {
+    const int nout = rows * o2n * sh.O3;
+    const int SL = (nout + p.CL - 1) / p.CL;
+    const int ebeg = crank * SL, eend = min(nout, ebeg + SL);
+    for (int e = ebeg + tid; e < eend; e += kTcThreads) {
+      const int o3 = e % sh.O3, q = e / sh.O3;
+      const int o = q % o2n, r = q / o2n;
+      const int idx = r * ystr + o * sh.O3 + o3;
+      float sum = 0.f;
+      for (int k = 0; k < p.CL; ++k) sum += peer(k)[idx];
+      if (p.NC > 1) {
+        slot[e] = sum;
+      } else {
         const int t = r / sh.O1, o1 = r - t * sh.O1;
         y[(size_t)t * sh.d_out + o1 * sh.sy1 + (o2a + o) * sh.sy2 + o3 * sh.sy3] =
             from_f32<E>(sum);
       }
-      if (tid == 0) atomicExch(counter, 0);
+    }
+    if (p.CL > 1) cluster.sync();  // peers finished reading this CTA's shared memory
+    if (p.NC > 1) {
+      __threadfence();
+      __syncthreads();
+      int* counter = p.cnt + ((size_t)tile * p.NG + grp) * p.CL + crank;
+      if (tid == 0) *flag = (atomicAdd(counter, 1) == p.NC - 1);
+      __syncthreads();
+      if (*flag) {  // last cluster for this slice: add the NC slots in cluster order, write y
+        __threadfence();
+        for (int e = ebeg + tid; e < eend; e += kTcThreads) {
+          float sum = 0.f;
+          for (int c = 0; c < p.NC; ++c) sum += __ldcg(s0 + (size_t)c * p.slot_elems + e);
+          const int o3 = e % sh.O3, q = e / sh.O3;
+          const int o = q % o2n, r = q / o2n;
+          const int t = r / sh.O1, o1 = r - t * sh.O1;
+          y[(size_t)t * sh.d_out + o1 * sh.sy1 + (o2a + o) * sh.sy2 + o3 * sh.sy3] =
+              from_f32<E>(sum);
+        }
+        if (tid == 0) atomicExch(counter, 0);
+      }
     }
   }
 }
@@ -590,7 +802,7 @@ static void fill_tc(TcParams<S>& tp, const Plan& p, const TcGeom& g, const void*
   const TcLayout& t = p.t;
   tp.x = x;
   tp.y = y;
-  tp.g1f = reinterpret_cast<const uint2*>(base + p.m.off_g1);
+  tp.b1 = reinterpret_cast<const unsigned char*>(base + t.off_b1);
   tp.b2 = reinterpret_cast<const unsigned char*>(base + t.off_b2);
   tp.b3 = reinterpret_cast<const unsigned char*>(base + t.off_b3);
   const size_t counters = ((size_t)g.ntiles * t.NG * g.CL * sizeof(int) + 255) / 256 * 256;
@@ -599,29 +811,42 @@ static void fill_tc(TcParams<S>& tp, const Plan& p, const TcGeom& g, const void*
   tp.slots = reinterpret_cast<float*>(static_cast<char*>(ws) + 256 + counters);
   tp.T = (int)T;
   tp.TT = g.TT;
-  tp.MT1 = g.MT1;
   tp.CL = g.CL;
   tp.NC = g.NC;
   tp.NG = t.NG;
   tp.O2G = t.O2G;
+  tp.shared_d12 = t.shared_d12;
+  tp.ND1 = t.ND1;
+  tp.DBW = t.DBW;
+  tp.N1P = t.N1P;
   tp.N2 = t.N2;
   tp.N3P = t.N3P;
-  tp.K3P = t.K3P;
+  tp.d2_col = t.d2_col;
+  tp.d3_col = t.d3_col;
   tp.tmem_cols = t.tmem_cols;
-  tp.g1p_bytes = p.m.KS1 * p.m.NT1 * 256;
+  tp.b1_bytes = (int)t.bytes_b1_slice;
   tp.b2_bytes = (int)t.bytes_b2_group;
-  tp.b3p_bytes = (int)t.bytes_b3_piece;
-  tp.off_xs = (int)g.off_xs;
+  tp.b3_bytes = (int)t.bytes_b3_piece;
   tp.off_a2 = (int)g.off_a2;
   tp.off_b2 = (int)g.off_b2;
   tp.off_a3 = (int)g.off_a3;
-  tp.off_g1 = (int)g.off_pbuf;
-  tp.off_b3 = (int)(g.off_pbuf + 4 * (size_t)tp.g1p_bytes);
+  tp.off_a1 = (int)g.off_a1;
+  tp.off_g1 = (int)g.off_g1;
+  tp.off_b3 = (int)g.off_b3;
   tp.off_bar = (int)g.off_bar;
   tp.NA2 = g.NA2;
+  tp.NA3 = g.NA3;
+  tp.NB1 = g.NB1;
+  tp.b1_all = g.b1_all;
+  tp.NB3 = g.NB3;
+  tp.b3_all = g.b3_all;
   tp.a2_bytes = (int)g.a2_bytes;
-  tp.a3_bytes = (int)(t.O2G * 128 * t.K3P * 2);
-  tp.a2_sbo = (p.m.K2P / 8) * kA2Lbo;
+  tp.a3_bytes = (int)g.a3_bytes;
+  tp.a1_bytes = (int)g.a1_bytes;
+  tp.ystr = g.ystr;
+  const Canon& c = p.c;
+  tp.vec_out = c.sy3 == 1 && c.O3 % 8 == 0 && c.sy1 % 8 == 0 && c.sy2 % 8 == 0 &&
+               c.d_out % 8 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
   tp.slot_elems = 128 * t.O2G * p.c.O3;
 }
 
@@ -645,20 +870,19 @@ static bool shape_is(const Plan& p) {
 template <typename E>
 static cudaError_t launch_tc_e(const Plan& p, const TcGeom& g, const void* packed, const void* x,
                                int64_t T, void* y, void* ws, int grid, cudaStream_t st) {
-#define TRR_TRY_TC(a, b, c, d, e, f, r, X, Y)                                               \
-  if (shape_is<FixedShape<a, b, c, d, e, f, r, X, Y>>(p))                                 \
-    return launch_tc_fixed<FixedShape<a, b, c, d, e, f, r, X, Y>, E>(p, g, packed, x, T, y, ws, \
-                                                                     grid, st);
+#define TRR_TRY_TC(a, b, c, d, e, f, r, X, Y)                                                    \
+  if constexpr (FixedShape<a, b, c, d, e, f, r, X, Y>::RPc <= 16) {                             \
+    if (shape_is<FixedShape<a, b, c, d, e, f, r, X, Y>>(p))                                     \
+      return launch_tc_fixed<FixedShape<a, b, c, d, e, f, r, X, Y>, E>(p, g, packed, x, T, y,   \
+                                                                       ws, grid, st);          \
+  }
   TRR_FIXED_SHAPES(TRR_TRY_TC)
 #undef TRR_TRY_TC
   TcParams<DynShape> tp;
   tp.sh = dyn_shape(p);
   fill_tc(tp, p, g, packed, x, T, y, ws);
-  switch (p.m.RP) {
-    case 8: return launch_tc_variant<DynShape, E, 8>(tp, g, p.device, grid, st);
-    case 16: return launch_tc_variant<DynShape, E, 16>(tp, g, p.device, grid, st);
-    default: return launch_tc_variant<DynShape, E, 32>(tp, g, p.device, grid, st);
-  }
+  if (p.m.RP == 8) return launch_tc_variant<DynShape, E, 8>(tp, g, p.device, grid, st);
+  return launch_tc_variant<DynShape, E, 16>(tp, g, p.device, grid, st);
 }
 
 int launch_tc05(const Plan& p, const TcGeom& g, const void* packed, const void* x, int64_t T,

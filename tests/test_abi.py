@@ -120,9 +120,12 @@ def test_geometry_and_workspace():
     assert p.workspace_bytes(0) == 0
     for T in (2, 8, 32, 33, 1000):
         t = p.tiling(T)
-        assert t.kernel == abi.KERNEL_MMA
+        assert t.kernel == abi.KERNEL_TC05       # tensor-core kernel once T * o1 > 16
         ws = p.workspace_bytes(T)
-        assert (ws > 0) == (t.clusters > 1)
+        assert ws >= 256                         # status word (+ counters)
+        assert (ws > 256 + 64 * 1024) == (t.clusters > 1)  # partial-sum slots across clusters
+        mma = abi.TrTiling(kernel=abi.KERNEL_MMA)
+        assert p.workspace_bytes(T, mma) >= 0
     forced = abi.TrTiling(tokens_per_tile=2, cluster=4, clusters=3, kernel=abi.KERNEL_MMA)
     assert p.workspace_bytes(5, forced) > 0
     bad = abi.TrTiling(tokens_per_tile=2, cluster=17, clusters=1, kernel=abi.KERNEL_MMA)

@@ -281,12 +281,16 @@ def test_tcgen05_geometries(golden, R, geom):
 
 
 @pytest.mark.parametrize("name,T,dtype", [
-    ("odd", 9, torch.float16), ("odd16", 20, torch.float16), ("c5", 16, torch.bfloat16),
-    ("c4_q", 24, torch.bfloat16), ("c4_gate", 8, torch.bfloat16), ("c2", 200, torch.float16)])
+    ("odd", 9, torch.float16), ("odd_cba", 31, torch.float16), ("odd_bac", 20, torch.float16),
+    ("odd_cab", 17, torch.bfloat16), ("c5", 16, torch.bfloat16), ("c4_q", 24, torch.bfloat16),
+    ("c4_gate", 8, torch.bfloat16), ("c4_down", 9, torch.bfloat16), ("c2", 200, torch.float16)])
 def test_tcgen05_shapes_against_oracle(name, T, dtype):
     s = {"odd": kspec.TRSpec((2, 3, 4), (5, 6, 7), 3),
-         "odd16": kspec.TRSpec((8, 6, 20), (12, 5, 24), 16), "c5": kspec.SPEC_C5,
-         "c4_q": kspec.SPEC_C4["q"], "c4_gate": kspec.SPEC_C4["gate"], "c2": kspec.SPEC_C2}[name]
+         "odd_cba": kspec.TRSpec((6, 5, 12), (7, 6, 9), 11),
+         "odd_bac": kspec.TRSpec((5, 7, 6), (9, 3, 10), 13),
+         "odd_cab": kspec.TRSpec((4, 6, 10), (6, 11, 7), 9), "c5": kspec.SPEC_C5,
+         "c4_q": kspec.SPEC_C4["q"], "c4_gate": kspec.SPEC_C4["gate"],
+         "c4_down": kspec.SPEC_C4["down"], "c2": kspec.SPEC_C2}[name]
     cores = kspec.baseline_cores(s, seed=3, dtype=dtype, device=DEV)
     fn = prepare_optimized(cores, s)
     x = kspec.baseline_x(s, T, seed=3, dtype=dtype, device=DEV)
@@ -296,3 +300,15 @@ def test_tcgen05_shapes_against_oracle(name, T, dtype):
                                       [c.float().cpu().numpy() for c in cores])
     check_close(y, ref, dtype)
     torch.testing.assert_close(fn.call_tiled(x, abi.KERNEL_TC05), y, rtol=0, atol=0)
+
+
+def test_tcgen05_unsupported_shape_raises():
+    """O1 * RP above 256 S1 columns: the forced tcgen05 kernel reports UNSUPPORTED, the default
+    path serves the spec with another kernel."""
+    s = kspec.TRSpec((8, 6, 20), (12, 5, 24), 16)
+    fn = prepare_optimized(kspec.baseline_cores(s, device=DEV), s)
+    x = kspec.baseline_x(s, 40, device=DEV)
+    with pytest.raises(RuntimeError):
+        fn.call_tiled(x, abi.KERNEL_TC05)
+    assert fn.tiling(40)["kernel"] != abi.KERNEL_TC05
+    fn(x)

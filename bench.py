@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-dense", action="store_true")
+    ap.add_argument("--prefill-tokens", type=int, default=65536,
+                    help="tokens of the sharded prefill leg (config 5), split over the ranks; "
+                         "0 skips it")
     return ap.parse_args()
 
 
@@ -236,6 +239,63 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def prefill_leg(args, rank, world, dev, tc_peak):
+    """Config 5: 4096 -> 14336, modes (16,16,16)->(16,28,32), R16, bf16, `--prefill-tokens`
+    tokens split over the ranks (ShardedRing row split, cores replicated, no collective on the
+    data path).  Device time per call (CUDA events), max over ranks; one all_gather of y timed
+    separately when world > 1."""
+    from kernel_task_b200 import prepare_optimized
+    from kernel_task_b200.shard import ShardedRing, shard_bounds
+    from kernel_task_b200.spec import SPEC_C5, baseline_cores
+
+    T = args.prefill_tokens
+    a, b = shard_bounds(T, world, rank)
+    cores = baseline_cores(SPEC_C5, seed=0, dtype=torch.bfloat16, device=dev)
+    op = ShardedRing(cores, SPEC_C5, op_factory=prepare_optimized)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5000 + rank)
+    x = torch.randn(b - a, SPEC_C5.in_features, generator=gen, device=dev).to(torch.bfloat16)
+    for _ in range(2):
+        op.local(x)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    steps = max(1, min(args.steps, 3))
+    times = []
+    for _ in range(steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        y = op.local(x)
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = max_over_ranks([statistics.mean(times)], world)[0]
+    out = {"workload": "c5: 4096->14336 (16,16,16)->(16,28,32) R16 bf16, tokens split by rows, "
+                       "cores replicated per GPU",
+           "tokens": T, "tokens_per_rank_max": shard_bounds(T, world, 0)[1],
+           "ms": round(ms, 3), "tokens_per_s": round(T / (ms * 1e-3), 1),
+           "steps": steps, "scaling": "strong", "timing": "CUDA events, max over ranks"}
+    flops = op.fn.flops_per_token() * shard_bounds(T, world, 0)[1]
+    out["tflops_per_gpu"] = round(flops / (ms * 1e-3) / 1e12, 2)
+    out["frac_of_peak"] = round(flops / (ms * 1e-3) / 1e12 / tc_peak, 4)
+    if world > 1:
+        rows_max = shard_bounds(T, world, 0)[1]
+        padded = y.new_zeros((rows_max, SPEC_C5.out_features))
+        padded[: b - a] = y
+        parts = [torch.empty_like(padded) for _ in range(world)]
+        torch.distributed.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch.distributed.all_gather(parts, padded)
+        e1.record()
+        e1.synchronize()
+        out["gather_ms"] = round(max_over_ranks([e0.elapsed_time(e1)], world)[0], 3)
+        del parts, padded
+    del x, y, op
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, rank, world, local_rank):
     from kernel_task_b200 import prepare_optimized
     from kernel_task_b200.spec import TRSpec, baseline_cores, baseline_x
@@ -293,6 +353,8 @@ def run_ours(args, rank, world, local_rank):
         c["flops"] = c["fn"].flops_per_token() * c["x"].shape[0]
         c["tiling"] = c["fn"].tiling(c["x"].shape[0])
 
+    prefill = (prefill_leg(args, rank, world, dev, tc_peak) if args.prefill_tokens > 0
+               else None)
     keys = list(cases)
     med = max_over_ranks([statistics.median(cases[k]["cold"]) for k in keys], world)
     mean = max_over_ranks([statistics.mean(cases[k]["cold"]) for k in keys], world)
@@ -349,6 +411,8 @@ def run_ours(args, rank, world, local_rank):
                      "peak_kind": f"{peak_kind} bf16 dense (burst)"},
         "clocks": clk,
     }
+    if prefill is not None:
+        line["sharded_prefill"] = prefill
     if world == 1:
         value_cpu, threads, cpu_cases = cpu_reference_leg(1.0)
         line["cpu_baseline"] = {"value": round(value_cpu, 2), "unit": "us/call", "cores": threads,

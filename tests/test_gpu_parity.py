@@ -312,3 +312,20 @@ def test_tcgen05_unsupported_shape_raises():
         fn.call_tiled(x, abi.KERNEL_TC05)
     assert fn.tiling(40)["kernel"] != abi.KERNEL_TC05
     fn(x)
+
+
+def test_sharded_ring_single_process_matches_operator():
+    """ShardedRing without a process group is the whole operator (world 1): same bits."""
+    from kernel_task_b200.shard import ShardedRing
+    s = kspec.SPEC_C5
+    cores = kspec.baseline_cores(s, seed=2, dtype=torch.bfloat16, device=DEV)
+    op = ShardedRing(cores, s)
+    x = kspec.baseline_x(s, 300, seed=2, dtype=torch.bfloat16, device=DEV)
+    assert op.bounds(300) == (0, 300)
+    y = op(x)
+    torch.testing.assert_close(y, op(x, gather=True), rtol=0, atol=0)
+    torch.testing.assert_close(y, prepare_optimized(cores, s)(x), rtol=0, atol=0)
+    rows = torch.arange(0, 300, 37)
+    ref = oracle.tr_forward_reference(x[rows].float().cpu().numpy(),
+                                      [c.float().cpu().numpy() for c in cores])
+    check_close(y[rows], ref, torch.bfloat16)

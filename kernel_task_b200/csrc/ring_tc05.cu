@@ -12,21 +12,22 @@
 //   S3  D3[o2][(t,o1), o3] += A3[o2] . B3_piece[o3, v]                  (accumulated over pieces)
 // D1 and D2 live either in separate TMEM buffers (one or two D1, two D2) or, when that makes the
 // o2 groups wider, in two shared buffers that hold a piece's D1 and then its D2.
-// Roles (448 threads):
-//   warps 0-7   C1 (warps w and w+4 read the same TMEM lanes, each half of the o1 range); after
-//               each piece one C1 thread issues S2 of that piece and, with separate TMEM
-//               buffers, S1 of a later piece into the D1 buffer just read
-//   warps 8-11  C2; after each piece one C2 thread issues S3 of that piece and, with shared
-//               buffers, S1 of the piece two later into the buffer just read; then the D3
-//               read-out with warps 0-7
-//   warp 12     TMA loader: B2 once; B1 and B3 all at once when they fit, else rings refilled
-//               as the tensor-core stages release their slots
-//   warp 13     stages the x slice A1 of each further i3 (the first two are staged by everyone)
-// Each converter group synchronises on a named barrier before its thread issues, so a stage's
-// MMAs start as soon as their operands are written; the tensor-core stages signal their
-// consumers with one tcgen05.commit each (S1DONE, S2DONE, S3DONE).  After the last piece D3 is
-// summed across the cluster's CTAs through distributed shared memory (and across clusters
-// through workspace slots when NC > 1) and written as y.
+// Roles (480 threads):
+//   warps 0-7   C1 (warps w and w+4 read the same TMEM lanes, each half of the o1 range)
+//   warps 8-11  C2, and the D3 read-out with warps 0-7 after the last piece
+//   warp 12     issuer A: S2 of each piece, and S1 of a later piece into the D1 buffer C1 just
+//               read (separate TMEM buffers)
+//   warp 13     issuer B: S3 of each piece, and S1 of the piece two later into the buffer that
+//               held D2 (shared buffers)
+//   warp 14     feeder: B2, B1, B3 by TMA bulk copy (all at once when they fit, else rings
+//               refilled as the tensor-core stages release slots) and the x slice A1 of each
+//               further i3 (the first two are staged by the converter and feeder warps)
+// A converter group hands a finished piece to its issuer with a non-blocking bar.arrive on a
+// hardware named barrier (the issuer waits with bar.sync), so the converters never wait for MMA
+// issue; the tensor-core stages signal their consumers with one tcgen05.commit each (S1DONE,
+// S2DONE, S3DONE).  After the last piece D3 is summed across the cluster's CTAs through
+// distributed shared memory (and across clusters through workspace slots when NC > 1) and
+// written as y.
 //
 // Shared-memory operand layouts (K-major):
 //   A2  128-byte swizzle: 64-element K slabs of 128 rows x 128 B, row groups 1024 B apart, the
@@ -51,8 +52,11 @@ namespace cg = cooperative_groups;
 
 namespace trr {
 
-constexpr int kTcThreads = 448;
-constexpr int kBuildThreads = 416;  // every warp but the loader: first x slices
+constexpr int kTcThreads = 480;
+constexpr int kBuildThreads = 416;  // converter and feeder warps: first x slices
+// named barriers: 0 __syncthreads, 1 first x slices, 2-3 C1 -> issuer A, 4-5 C2 -> issuer B
+// (alternating by piece, so a producer can never run a generation ahead of its consumer)
+constexpr int kBarBuild = 1, kBarC1Done = 2, kBarC2Done = 4;
 constexpr unsigned kWaitLimit = 1u << 16;   // try_wait rounds before a wait gives up
 constexpr unsigned kSuspendNs = 20000;       // suspend-time hint of one try_wait round
 constexpr unsigned kPollLimit = 1u << 24;    // loader polls without progress before it gives up
@@ -198,9 +202,13 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       : "memory");
 }
 
-// Named barrier `id` over the first `n` threads that reach it (a multiple of 32).
+// Named barrier `id` over `n` threads (a multiple of 32): wait for all of them ...
 __device__ __forceinline__ void named_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory");
+}
+// ... or arrive without waiting (the producer side of a producer -> consumer hand-off).
+__device__ __forceinline__ void named_arrive(int id, int n) {
+  asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(n) : "memory");
 }
 
 template <int N>
@@ -377,8 +385,74 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   };
 
   if (warp == 12) {
-    // ============================ TMA loader ============================
-    if (lane == 0 && np > 0) {
+    // ===================== issuer A: S2 of each piece (and S1, separate buffers) ==============
+    bool ok = true, b2ok = false;
+    if (lane == 0 && np > 0) {  // the first S1s: as many as there are D1 buffers
+      const int first = p.shared_d12 ? 2 : p.ND1;
+      for (int k = 0; k < first && k < np && ok; ++k) ok = issue_s1(k);
+    }
+    for (int j = 0; j < np; ++j) {
+      named_sync(kBarC1Done + (j & 1), 256 + 32);  // C1(j): all of D1(j) read, A2(j) written
+      if (lane == 0 && ok && !*abort) {
+        tc_fence_after();
+        if (!b2ok) ok = b2ok = mbar_wait(bar(BAR_B2FULL), 0, abort);
+        if (ok && !p.shared_d12 && j >= 2)  // C2 read D2(j - 2) from this buffer
+          ok = mbar_wait(bar(BAR_D2FREE + (j & 1)), ((j >> 1) - 1) & 1, abort);
+        if (ok) {
+          tc_fence_after();
+          const uint32_t a2 = a2s + (j % p.NA2) * p.a2_bytes;
+          const uint32_t sbo2 = (uint32_t)(sh.K2P / 8) * 128;
+          const uint32_t idesc2 = umma_idesc<__half>(128, p.N2);
+          for (int ks = 0; ks < sh.KS2; ++ks)
+            umma(tmem + d2_col(j), desc_sw128(a2 + (ks >> 2) * kA2Slab + (ks & 3) * 32),
+                 desc_plain(b2s + ks * 256, 128, sbo2), idesc2, ks > 0 ? 1u : 0u);
+          umma_commit(bar(BAR_S2DONE + (j & 1)));
+        }
+        // S1(j + ND1) into the D1 buffer C1 just read (separate arrangement)
+        if (ok && !p.shared_d12 && j + p.ND1 < np) ok = issue_s1(j + p.ND1);
+      }
+      __syncwarp();
+    }
+    if (lane == 0 && *abort) {  // drain this thread's tensor-core work
+      umma_commit(bar(BAR_DRAIN));
+      mbar_drain(bar(BAR_DRAIN), 0);
+    }
+    __syncwarp();
+  } else if (warp == 13) {
+    // ===================== issuer B: S3 of each piece (and S1, shared buffers) ================
+    bool ok = true;
+    for (int j = 0; j < np; ++j) {
+      named_sync(kBarC2Done + (j & 1), 128 + 32);  // C2(j): all of D2(j) read, A3(j) written
+      if (lane == 0 && ok && !*abort) {
+        tc_fence_after();
+        ok = p.b3_all ? mbar_wait(bar(BAR_B3FULL), 0, abort)
+                      : mbar_wait(bar(BAR_B3FULL + (j & 3)), (j >> 2) & 1, abort);
+        if (ok) {
+          tc_fence_after();
+          const uint32_t a3 = a3s + (j % p.NA3) * p.a3_bytes;
+          const uint32_t b3 = b3s + (p.b3_all ? j : (j & 3)) * p.b3_bytes;
+          const uint32_t sbo3 = (uint32_t)(K3 / 8) * 128;
+          const uint32_t idesc3 = umma_idesc<__half>(128, p.N3P);
+          for (int o = 0; o < o2n; ++o)
+            umma(tmem + p.d3_col + o * p.N3P, desc_plain(a3 + o * a3_block, 128, sbo3),
+                 desc_plain(b3, 128, sbo3), idesc3, j > 0 ? 1u : 0u);
+          umma_commit(bar(BAR_S3DONE + (j & 3)));
+          if (j == np - 1) umma_commit(bar(BAR_D3DONE));
+        }
+        // S1(j + 2) into the buffer that held D2(j) (shared arrangement)
+        if (ok && p.shared_d12 && j + 2 < np) ok = issue_s1(j + 2);
+      }
+      __syncwarp();
+    }
+    if (lane == 0 && *abort) {  // drain this thread's tensor-core work
+      umma_commit(bar(BAR_DRAIN + 1));
+      mbar_drain(bar(BAR_DRAIN + 1), 0);
+    }
+    __syncwarp();
+  } else {
+    // ---- first x slices, staged by the converter and feeder warps
+    const int bt = tid < 384 ? tid : tid - 64;
+    if (np > 0 && warp == 14 && lane == 0) {  // the feeder's first bulk copies go out at once
       bulk_load(b2s, p.b2 + (size_t)grp * p.b2_bytes, p.b2_bytes, bar(BAR_B2FULL));
       if (p.b1_all) {
         bulk_load(g1s, p.b1, sh.R * p.b1_bytes, bar(BAR_G1FULL));
@@ -394,66 +468,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
           bulk_load(b3s + q * p.b3_bytes, p.b3 + (size_t)(pa + q) * p.b3_bytes, p.b3_bytes,
                     bar(BAR_B3FULL + q));
       }
-      // rings: refill a slot once the S1 / S3 of the piece NB1 / 4 earlier has completed
-      int r1 = p.b1_all ? np : min(NB1, np), r3 = p.b3_all ? np : min(4, np);
-      unsigned idle = 0;
-      while ((r1 < np || r3 < np) && !*abort) {
-        bool prog = false;
-        if (r1 < np && mbar_test(bar(BAR_S1DONE + ((r1 - NB1) & 3)), ((r1 - NB1) >> 2) & 1)) {
-          bulk_load(g1s + (r1 % NB1) * p.b1_bytes, p.b1 + (size_t)((pa + r1) % sh.R) * p.b1_bytes,
-                    p.b1_bytes, bar(BAR_G1FULL + r1 % NB1));
-          ++r1;
-          prog = true;
-        }
-        if (r3 < np && mbar_test(bar(BAR_S3DONE + ((r3 - 4) & 3)), ((r3 - 4) >> 2) & 1)) {
-          bulk_load(b3s + (r3 & 3) * p.b3_bytes, p.b3 + (size_t)(pa + r3) * p.b3_bytes, p.b3_bytes,
-                    bar(BAR_B3FULL + (r3 & 3)));
-          ++r3;
-          prog = true;
-        }
-        if (prog) {
-          idle = 0;
-        } else if (++idle >= kPollLimit) {
-          *abort = 1;
-        } else {
-          __nanosleep(64);
-        }
-      }
-      if (*abort) {  // drain this CTA's bulk copies before leaving
-        mbar_drain(bar(BAR_B2FULL), 0);
-        if (p.b1_all) mbar_drain(bar(BAR_G1FULL), 0);
-        else
-          for (int q = max(0, r1 - NB1); q < r1; ++q)
-            mbar_drain(bar(BAR_G1FULL + q % NB1), (q / NB1) & 1);
-        if (p.b3_all) mbar_drain(bar(BAR_B3FULL), 0);
-        else
-          for (int q = max(0, r3 - 4); q < r3; ++q) mbar_drain(bar(BAR_B3FULL + (q & 3)), (q >> 2) & 1);
-      }
     }
     __syncwarp();
-  } else {
-    // ---- first x slices, staged by every thread but the loader's
-    const int bt = tid < 384 ? tid : tid - 32;
     for (int q = 0; q < 2 && q < nq; ++q)
       build_a1(sh, smem + p.off_a1 + q * p.a1_bytes, xt, TTv, i3a + q, bt, kBuildThreads);
     fence_async_smem();
-    named_sync(1, kBuildThreads);
+    named_sync(kBarBuild, kBuildThreads);
     if (tid == 0)
       for (int q = 0; q < 2 && q < nq; ++q) mbar_arrive(bar(BAR_A1FULL + q));
 
     if (warp < 8) {
-      // ============================ C1: D1 -> A2, issues S2 (and S1) ============================
+      // ============================ C1: D1 -> A2 ============================
       const int r1 = 32 * (warp & 3) + lane;  // D1 row (t, i2)
       const int tq = r1 / sh.I2, i2 = r1 - tq * sh.I2;
       const bool rvalid = tq < p.TT;
       const int h = (sh.O1 + 1) >> 1;
       const int o1a = (warp >> 2) ? h : 0, o1b = (warp >> 2) ? sh.O1 : h;
       const int rot = NCH == 2 ? ((i2 >> 2) & 1) : 0;
-      bool ok = true, b2ok = false;
-      if (tid == 0) {  // the first S1s: as many as there are D1 buffers
-        const int first = p.shared_d12 ? 2 : p.ND1;
-        for (int k = 0; k < first && k < np && ok; ++k) ok = issue_s1(k);
-      }
+      bool ok = true;
       for (int j = 0; j < np; ++j) {
         const int ab = j % p.NA2;
         if (ok) ok = mbar_wait(bar(BAR_S1DONE + (j & 3)), (j >> 2) & 1, abort);
@@ -489,33 +521,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
           fence_async_smem();
         }
         tc_fence_before();
-        named_sync(2, 256);  // all of D1(j) read, all of A2(j) written
-        if (tid == 0 && ok && !*abort) {
-          tc_fence_after();
-          // ---- S2(j): D2 buffer drained by C2 (separate arrangement), B2 landed
-          if (!b2ok) ok = b2ok = mbar_wait(bar(BAR_B2FULL), 0, abort);
-          if (ok && !p.shared_d12 && j >= 2)
-            ok = mbar_wait(bar(BAR_D2FREE + (j & 1)), ((j >> 1) - 1) & 1, abort);
-          if (ok) {
-            tc_fence_after();
-            const uint32_t a2 = a2s + ab * p.a2_bytes;
-            const uint32_t sbo2 = (uint32_t)(sh.K2P / 8) * 128;
-            const uint32_t idesc2 = umma_idesc<__half>(128, p.N2);
-            for (int ks = 0; ks < sh.KS2; ++ks)
-              umma(tmem + d2_col(j), desc_sw128(a2 + (ks >> 2) * kA2Slab + (ks & 3) * 32),
-                   desc_plain(b2s + ks * 256, 128, sbo2), idesc2, ks > 0 ? 1u : 0u);
-            umma_commit(bar(BAR_S2DONE + (j & 1)));
-          }
-          // ---- S1(j + ND1) into the D1 buffer just read (separate arrangement)
-          if (ok && !p.shared_d12 && j + p.ND1 < np) ok = issue_s1(j + p.ND1);
-        }
-      }
-      if (tid == 0 && *abort) {  // drain this thread's tensor-core work
-        umma_commit(bar(BAR_DRAIN));
-        mbar_drain(bar(BAR_DRAIN), 0);
+        named_arrive(kBarC1Done + (j & 1), 256 + 32);  // hand piece j to issuer A
       }
     } else if (warp < 12) {
-      // ============================ C2: D2 -> A3, issues S3 (and S1) ============================
+      // ============================ C2: D2 -> A3 ============================
       const int r = 32 * (warp & 3) + lane;  // row (t, o1)
       bool ok = true;
       for (int j = 0; j < np; ++j) {
@@ -534,7 +543,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
             for (int c = 0; c < 4; ++c)
               if (c0 + c * 16 < p.N2) tmem_ld<16>(d2 + c0 + c * 16, v[c]);
             tmem_wait_ld();
-            if (!p.shared_d12 && c0 + 64 >= p.N2) {  // last read of D2: C1 may reuse the buffer
+            if (!p.shared_d12 && c0 + 64 >= p.N2) {  // last read of D2: S2 may reuse the buffer
               tc_fence_before();
               __syncwarp();
               if (lane == 0) mbar_arrive(bar(BAR_D2FREE + db));
@@ -558,44 +567,64 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
           if (lane == 0) mbar_arrive(bar(BAR_D2FREE + db));
         }
         tc_fence_before();
-        named_sync(3, 128);  // all of D2(j) read, all of A3(j) written
-        if (tid == 256 && ok && !*abort) {
-          tc_fence_after();
-          // ---- S3(j): B3 landed
-          ok = p.b3_all ? mbar_wait(bar(BAR_B3FULL), 0, abort)
-                        : mbar_wait(bar(BAR_B3FULL + (j & 3)), (j >> 2) & 1, abort);
-          if (ok) {
-            tc_fence_after();
-            const uint32_t a3 = a3s + ab * p.a3_bytes;
-            const uint32_t b3 = b3s + (p.b3_all ? j : (j & 3)) * p.b3_bytes;
-            const uint32_t sbo3 = (uint32_t)(K3 / 8) * 128;
-            const uint32_t idesc3 = umma_idesc<__half>(128, p.N3P);
-            for (int o = 0; o < o2n; ++o)
-              umma(tmem + p.d3_col + o * p.N3P, desc_plain(a3 + o * a3_block, 128, sbo3),
-                   desc_plain(b3, 128, sbo3), idesc3, j > 0 ? 1u : 0u);
-            umma_commit(bar(BAR_S3DONE + (j & 3)));
-            if (j == np - 1) umma_commit(bar(BAR_D3DONE));
-          }
-          // ---- S1(j + 2) into the buffer that held D2(j) (shared arrangement)
-          if (ok && p.shared_d12 && j + 2 < np) ok = issue_s1(j + 2);
-        }
-      }
-      if (tid == 256 && *abort) {  // drain this thread's tensor-core work
-        umma_commit(bar(BAR_DRAIN + 1));
-        mbar_drain(bar(BAR_DRAIN + 1), 0);
+        named_arrive(kBarC2Done + (j & 1), 128 + 32);  // hand piece j to issuer B
       }
     } else {
-      // ============================ x slices of further i3 ============================
-      bool ok = true;
-      for (int q = 2; q < nq; ++q) {
-        if (ok) ok = mbar_wait(bar(BAR_A1FREE + (q & 1)), ((q >> 1) - 1) & 1, abort);
-        if (ok) {
+      // ==================== feeder: ring refills and the x slices of further i3 ================
+      // Polls; every decision is taken by all lanes together (a vote over their own tests).
+      int r1 = p.b1_all ? np : min(NB1, np), r3 = p.b3_all ? np : min(4, np), q = 2;
+      unsigned idle = 0;
+      while ((q < nq || r1 < np || r3 < np) && !*abort) {
+        bool prog = false;
+        if (q < nq && __all_sync(0xffffffffu,
+                                 mbar_test(bar(BAR_A1FREE + (q & 1)), ((q >> 1) - 1) & 1))) {
           build_a1(sh, smem + p.off_a1 + (q & 1) * p.a1_bytes, xt, TTv, i3a + q, lane, 32);
           fence_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(BAR_A1FULL + (q & 1)));
+          ++q;
+          prog = true;
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(BAR_A1FULL + (q & 1)));
+        if (r1 < np && __all_sync(0xffffffffu, mbar_test(bar(BAR_S1DONE + ((r1 - NB1) & 3)),
+                                                         ((r1 - NB1) >> 2) & 1))) {
+          if (lane == 0)
+            bulk_load(g1s + (r1 % NB1) * p.b1_bytes,
+                      p.b1 + (size_t)((pa + r1) % sh.R) * p.b1_bytes, p.b1_bytes,
+                      bar(BAR_G1FULL + r1 % NB1));
+          __syncwarp();
+          ++r1;
+          prog = true;
+        }
+        if (r3 < np && __all_sync(0xffffffffu, mbar_test(bar(BAR_S3DONE + ((r3 - 4) & 3)),
+                                                         ((r3 - 4) >> 2) & 1))) {
+          if (lane == 0)
+            bulk_load(b3s + (r3 & 3) * p.b3_bytes, p.b3 + (size_t)(pa + r3) * p.b3_bytes,
+                      p.b3_bytes, bar(BAR_B3FULL + (r3 & 3)));
+          __syncwarp();
+          ++r3;
+          prog = true;
+        }
+        if (prog) {
+          idle = 0;
+        } else if (++idle >= kPollLimit) {
+          if (lane == 0) *abort = 1;
+          __syncwarp();
+        } else {
+          __nanosleep(64);
+        }
       }
+      if (lane == 0 && np > 0 && *abort) {  // drain this CTA's bulk copies before leaving
+        mbar_drain(bar(BAR_B2FULL), 0);
+        if (p.b1_all) mbar_drain(bar(BAR_G1FULL), 0);
+        else
+          for (int k = max(0, r1 - NB1); k < r1; ++k)
+            mbar_drain(bar(BAR_G1FULL + k % NB1), (k / NB1) & 1);
+        if (p.b3_all) mbar_drain(bar(BAR_B3FULL), 0);
+        else
+          for (int k = max(0, r3 - 4); k < r3; ++k)
+            mbar_drain(bar(BAR_B3FULL + (k & 3)), (k >> 2) & 1);
+      }
+      __syncwarp();
     }
   }
 

@@ -96,8 +96,8 @@ static void build_mma_layout(Plan* p) {
 // Shared memory of one tcgen05 CTA (ring_tc05.cu), relative to a 1024-byte aligned base:
 //   A2 x NA2 (S2 A operand, 128-byte swizzle, 64-wide K slabs of 128 rows), B2 of the group,
 //   A3 x NA3 (S3 A operands of the group's o2), A1 x 2 (x slices), B1 x NB1, B3 x NB3,
-// reused after the piece loop as the CTA's fp32 partial y [128 rows x ystr], then the
-// mbarriers.  `total` includes 1 KB of slack for aligning the dynamic shared-memory window.
+// reused after the piece loop as the CTA's fp32 partial y [128 rows x ystr] and the receive
+// buffers of the cluster reduction, then the mbarriers.  `total` includes 1 KB of slack for aligning the dynamic shared-memory window.
 struct TcSmem {
   size_t a2_bytes, a3_bytes, a1_bytes;
   size_t off_a2, off_b2, off_a3, off_a1, off_g1, off_b3, off_bar, total;
@@ -128,8 +128,10 @@ static TcSmem tc_smem(const Plan& p, int O2G, int NA2, int NA3, int NB1, int NB3
   s.off_g1 = align_up(s.off_a1 + 2 * s.a1_bytes, 128);
   s.off_b3 = align_up(s.off_g1 + NB1 * b1, 128);
   const size_t main = s.off_b3 + NB3 * b3;
+  // partial y, then the cluster-reduction receive buffers (at most the same size + 16 items)
   const size_t ys = (size_t)128 * tc_ystr(p, O2G) * 4;
-  s.off_bar = align_up(std::max(main, ys), 128);
+  const size_t recv = ys + 16 * 32;
+  s.off_bar = align_up(std::max(main, ys + recv), 128);
   s.total = s.off_bar + 512 + 1024;
   return s;
 }
@@ -413,9 +415,11 @@ int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* f, TcGeom* g) {
     CL = f->cluster;
     NC = f->clusters > 0 ? f->clusters : 1;
   } else {
+    // one wave of CTAs, but at least ~5 pieces per CTA: below that the fixed prologue and
+    // reduction cost more than the extra parallelism saves
     const long long cols = std::max<long long>(1, (long long)g->ntiles * t.NG);
     int NJ = cols >= p.num_sms ? 1 : (int)std::max<long long>(1, p.num_sms / cols);
-    NJ = std::min(NJ, m.npieces);
+    NJ = std::min(NJ, std::max(1, m.npieces / 5));
     CL = std::min(16, NJ);
     NC = std::max(1, NJ / CL);
   }
@@ -426,7 +430,7 @@ int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* f, TcGeom* g) {
   g->CL = CL;
   g->NC = NC;
   // buffer depths, deepest first: A2, A3 double; B1 all R slices, else a ring; B3 the CTA's
-  // whole piece range (at most 64 pieces), else a ring of 4
+  // whole piece range (at most 64 pieces), else a ring of 16, 8 or 4
   const int NJ = CL * NC;
   const int max_np = (m.npieces + NJ - 1) / NJ;
   TcSmem sm{};
@@ -437,9 +441,11 @@ int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* f, TcGeom* g) {
       for (int i1 = 0; i1 < 4 && !fits; ++i1) {
         const int nb1 = b1_opts[i1];
         if (i1 > 0 && nb1 >= c.R) continue;
-        for (int i3 = 0; i3 < 2 && !fits; ++i3) {
-          const int nb3 = i3 == 0 ? max_np : 4;
+        const int b3_opts[4] = {max_np, 16, 8, 4};
+        for (int i3 = 0; i3 < 4 && !fits; ++i3) {
+          const int nb3 = b3_opts[i3];
           if (i3 == 0 && max_np > 64) continue;
+          if (i3 > 0 && nb3 >= max_np) continue;
           sm = tc_smem(p, t.O2G, na2, na3, nb1, nb3);
           if (sm.total <= p.smem_optin) {
             fits = true;

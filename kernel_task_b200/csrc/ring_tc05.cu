@@ -22,10 +22,11 @@
 //   warp 14     feeder: B2, B1, B3 by TMA bulk copy (all at once when they fit, else rings
 //               refilled as the tensor-core stages release slots) and the x slice A1 of each
 //               further i3 (the first two are staged by the converter and feeder warps)
-// A converter group hands a finished piece to its issuer with a non-blocking bar.arrive on a
-// hardware named barrier (the issuer waits with bar.sync), so the converters never wait for MMA
-// issue; the tensor-core stages signal their consumers with one tcgen05.commit each (S1DONE,
-// S2DONE, S3DONE).  After the last piece D3 is summed across the cluster's CTAs through
+// A converter group hands its work to the issuers through mbarriers (one arrival per warp): as
+// soon as its TMEM loads of a piece have landed (D1READ, D2READ: the accumulator buffer may be
+// overwritten by the next S1) and when the piece's operand is written (C1DONE, C2DONE).  The
+// issuers start the next S1 first, so the converters never wait for MMA issue; the tensor-core
+// stages signal their consumers with one tcgen05.commit each (S1DONE, S2DONE, S3DONE).  After the last piece D3 is summed across the cluster's CTAs through
 // distributed shared memory (and across clusters through workspace slots when NC > 1) and
 // written as y.
 //
@@ -54,9 +55,7 @@ namespace trr {
 
 constexpr int kTcThreads = 480;
 constexpr int kBuildThreads = 416;  // converter and feeder warps: first x slices
-// named barriers: 0 __syncthreads, 1 first x slices, 2-3 C1 -> issuer A, 4-5 C2 -> issuer B
-// (alternating by piece, so a producer can never run a generation ahead of its consumer)
-constexpr int kBarBuild = 1, kBarC1Done = 2, kBarC2Done = 4;
+constexpr int kBarBuild = 1;  // named barrier of the first x slices (0 is __syncthreads)
 constexpr unsigned kWaitLimit = 1u << 16;   // try_wait rounds before a wait gives up
 constexpr unsigned kSuspendNs = 20000;       // suspend-time hint of one try_wait round
 constexpr unsigned kPollLimit = 1u << 24;    // loader polls without progress before it gives up
@@ -68,13 +67,16 @@ enum {
   BAR_G1FULL = 4,   // [4] B1 landed (slot 0 only when all slices load at once)
   BAR_S1DONE = 8,   // [4] commit after S1(j), index j % 4
   BAR_S2DONE = 12,  // [2] commit after S2(j), index j % 2
-  BAR_D2FREE = 14,  // [2] separate TMEM arrangement: C2 warps read D2 (count 4)
-  BAR_S3DONE = 16,  // [4] commit after S3(j), index j % 4
-  BAR_B3FULL = 20,  // [4] B3 landed (slot 0 only when the whole range loads at once)
-  BAR_B2FULL = 24,  // B2 landed
-  BAR_D3DONE = 25,  // commit after the last S3: every tensor-core operation completed
-  BAR_DRAIN = 26,   // [2] after a timeout: the two issuing threads' own work completed
-  BAR_COUNT = 28
+  BAR_D2READ = 14,  // [2] C2 warps read D2(j) (count 4), index j % 2
+  BAR_S3DONE = 16,  // [16] commit after S3(j), index j % 16
+  BAR_B3FULL = 32,  // [16] B3 landed (slot 0 only when the whole range loads at once)
+  BAR_B2FULL = 48,  // B2 landed
+  BAR_D3DONE = 49,  // commit after the last S3: every tensor-core operation completed
+  BAR_DRAIN = 50,   // [2] after a timeout: the two issuing warps' own work completed
+  BAR_C1DONE = 52,  // [2] C1 warps finished piece j (count 8), index j % 2
+  BAR_C2DONE = 54,  // [2] C2 warps finished piece j (count 4), index j % 2
+  BAR_D1READ = 56,  // [2] C1 warps read D1(j) (count 8), index j % 2
+  BAR_COUNT = 58
 };
 
 template <class S>
@@ -93,7 +95,7 @@ struct TcParams {
   int b1_bytes, b2_bytes, b3_bytes;
   int off_a2, off_b2, off_a3, off_a1, off_g1, off_b3, off_bar;
   int NA2, NA3, NB1, b1_all, NB3, b3_all, a2_bytes, a3_bytes, a1_bytes;
-  int ystr, vec_out, slot_elems;
+  int ystr, recv_off, vec_out, slot_elems;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -118,20 +120,24 @@ __host__ __device__ constexpr uint32_t umma_idesc(int M, int N) {
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma(uint32_t dtmem, uint64_t da, uint64_t db, uint32_t idesc,
-                                     uint32_t accumulate) {
+// tcgen05.mma, issued by one elected lane of a converged warp: every lane executes the call with
+// the same operands, so the descriptor arithmetic stays warp-uniform.
+__device__ __forceinline__ void umma_one(uint32_t dtmem, uint64_t da, uint64_t db, uint32_t idesc,
+                                         uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(
+      "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(
           dtmem),
       "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
 }
-
-__device__ __forceinline__ void umma_commit(uint32_t mbar) {
+__device__ __forceinline__ void commit_one(uint32_t mbar) {
   asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(mbar)
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(
+          mbar)
       : "memory");
 }
+
 
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
@@ -177,6 +183,11 @@ __device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, volati
   }
   *abort = 1;
   return false;
+}
+
+// A converged warp waits together and agrees on the outcome.
+__device__ __forceinline__ bool warp_wait(uint32_t mbar, uint32_t parity, volatile int* abort) {
+  return __all_sync(0xffffffffu, mbar_wait(mbar, parity, abort));
 }
 
 // Bounded wait that ignores the abort flag: draining the CTA's own work in flight.
@@ -284,7 +295,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   const S& sh = p.sh;
   constexpr int K3 = 16;         // S3 K (v padded to 16)
   constexpr int NCH = RP / 8;    // 16-byte chunks of one (o1 or o2, i2) run of RP values
-  constexpr int OB = 64 / RP;    // o1 per TMEM batch in C1 (64 columns)
+  constexpr int OB = RP == 16 ? 5 : 8;  // o1 per TMEM batch in C1 (<= 80 columns, one wait)
+  constexpr int CB = 5;          // 16-column chunks per TMEM batch in C2
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -329,7 +341,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   }
   if (tid == 32) {
     for (int i = 0; i < BAR_COUNT; ++i) {
-      const int count = (i >= BAR_D2FREE && i < BAR_S3DONE) ? 4 : 1;
+      int count = 1;
+      if ((i >= BAR_D2READ && i < BAR_D2READ + 2) || (i >= BAR_C2DONE && i < BAR_C2DONE + 2))
+        count = 4;
+      if ((i >= BAR_C1DONE && i < BAR_C1DONE + 2) || (i >= BAR_D1READ && i < BAR_D1READ + 2))
+        count = 8;
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar(i)), "r"(count)
                    : "memory");
     }
@@ -362,91 +378,101 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   const uint32_t b3s = smem_u32(smem + p.off_b3);
   const int NB1 = p.NB1;
 
-  // S1(k) from one thread: waits for its x slice and B1, accumulates into D1(k), signals
-  // S1DONE (and A1FREE after the last piece of an i3).  False when a wait gave up.
+  // S1(k), issued by a converged warp: waits for its x slice and B1 (each only once when it
+  // does not change from piece to piece), accumulates into D1(k), signals S1DONE (and A1FREE
+  // after the last piece of an i3).  False when a wait gave up.
+  int s1_q_seen = -1;
+  bool s1_b1_seen = false;
   auto issue_s1 = [&](int k) -> bool {
     const int q = (pa + k) / sh.R - i3a;
-    bool ok = mbar_wait(bar(BAR_A1FULL + (q & 1)), (q >> 1) & 1, abort);
-    if (ok)
-      ok = p.b1_all ? mbar_wait(bar(BAR_G1FULL), 0, abort)
-                    : mbar_wait(bar(BAR_G1FULL + k % NB1), (k / NB1) & 1, abort);
+    bool ok = true;
+    if (q != s1_q_seen) {
+      ok = warp_wait(bar(BAR_A1FULL + (q & 1)), (q >> 1) & 1, abort);
+      s1_q_seen = q;
+    }
+    if (ok && !s1_b1_seen) {
+      ok = p.b1_all ? warp_wait(bar(BAR_G1FULL), 0, abort)
+                    : warp_wait(bar(BAR_G1FULL + k % NB1), (k / NB1) & 1, abort);
+      s1_b1_seen = p.b1_all;
+    }
     if (!ok) return false;
-    tc_fence_after();
     const uint32_t a1 = a1s + (q & 1) * p.a1_bytes;
     const uint32_t b1 = g1s + (p.b1_all ? (pa + k) % sh.R : k % NB1) * p.b1_bytes;
     const uint32_t sbo1 = (uint32_t)sh.KS1 * 256;
     const uint32_t idesc1 = umma_idesc<E>(128, p.N1P);
     for (int ks = 0; ks < sh.KS1; ++ks)
-      umma(tmem + d1_col(k), desc_plain(a1 + ks * 256, 128, sbo1),
-           desc_plain(b1 + ks * 256, 128, sbo1), idesc1, ks > 0 ? 1u : 0u);
-    umma_commit(bar(BAR_S1DONE + (k & 3)));
-    if (k == np - 1 || (pa + k + 1) % sh.R == 0) umma_commit(bar(BAR_A1FREE + (q & 1)));
+      umma_one(tmem + d1_col(k), desc_plain(a1 + ks * 256, 128, sbo1),
+               desc_plain(b1 + ks * 256, 128, sbo1), idesc1, ks > 0 ? 1u : 0u);
+    commit_one(bar(BAR_S1DONE + (k & 3)));
+    if (k == np - 1 || (pa + k + 1) % sh.R == 0) commit_one(bar(BAR_A1FREE + (q & 1)));
     return true;
   };
 
   if (warp == 12) {
     // ===================== issuer A: S2 of each piece (and S1, separate buffers) ==============
+    // The whole warp runs the loop (uniform decisions); one elected lane issues.
     bool ok = true, b2ok = false;
-    if (lane == 0 && np > 0) {  // the first S1s: as many as there are D1 buffers
+    if (np > 0) {  // the first S1s: as many as there are D1 buffers
       const int first = p.shared_d12 ? 2 : p.ND1;
       for (int k = 0; k < first && k < np && ok; ++k) ok = issue_s1(k);
     }
+    const uint32_t sbo2 = (uint32_t)(sh.K2P / 8) * 128;
+    const uint32_t idesc2 = umma_idesc<__half>(128, p.N2);
     for (int j = 0; j < np; ++j) {
-      named_sync(kBarC1Done + (j & 1), 256 + 32);  // C1(j): all of D1(j) read, A2(j) written
-      if (lane == 0 && ok && !*abort) {
-        tc_fence_after();
-        if (!b2ok) ok = b2ok = mbar_wait(bar(BAR_B2FULL), 0, abort);
-        if (ok && !p.shared_d12 && j >= 2)  // C2 read D2(j - 2) from this buffer
-          ok = mbar_wait(bar(BAR_D2FREE + (j & 1)), ((j >> 1) - 1) & 1, abort);
-        if (ok) {
-          tc_fence_after();
-          const uint32_t a2 = a2s + (j % p.NA2) * p.a2_bytes;
-          const uint32_t sbo2 = (uint32_t)(sh.K2P / 8) * 128;
-          const uint32_t idesc2 = umma_idesc<__half>(128, p.N2);
-          for (int ks = 0; ks < sh.KS2; ++ks)
-            umma(tmem + d2_col(j), desc_sw128(a2 + (ks >> 2) * kA2Slab + (ks & 3) * 32),
-                 desc_plain(b2s + ks * 256, 128, sbo2), idesc2, ks > 0 ? 1u : 0u);
-          umma_commit(bar(BAR_S2DONE + (j & 1)));
-        }
-        // S1(j + ND1) into the D1 buffer C1 just read (separate arrangement)
-        if (ok && !p.shared_d12 && j + p.ND1 < np) ok = issue_s1(j + p.ND1);
+      // No abort test in this loop: every wait checks the flag on its slow path, and an MMA
+      // issued after a timeout only computes values the caller discards.
+      // ---- S1(j + ND1) into the D1 buffer C1 has just read (separate arrangement)
+      if (ok && !p.shared_d12 && j + p.ND1 < np) {
+        ok = warp_wait(bar(BAR_D1READ + (j & 1)), (j >> 1) & 1, abort);
+        if (ok) ok = issue_s1(j + p.ND1);
       }
-      __syncwarp();
+      // ---- S2(j): C1(j) wrote A2(j); the D2 buffer's previous piece was read by C2
+      if (ok) ok = warp_wait(bar(BAR_C1DONE + (j & 1)), (j >> 1) & 1, abort);
+      if (ok && !b2ok) ok = b2ok = warp_wait(bar(BAR_B2FULL), 0, abort);
+      if (ok && !p.shared_d12 && j >= 2)
+        ok = warp_wait(bar(BAR_D2READ + (j & 1)), ((j >> 1) - 1) & 1, abort);
+      if (ok) {
+        const uint32_t a2 = a2s + (j % p.NA2) * p.a2_bytes;
+        for (int ks = 0; ks < sh.KS2; ++ks)
+          umma_one(tmem + d2_col(j), desc_sw128(a2 + (ks >> 2) * kA2Slab + (ks & 3) * 32),
+                   desc_plain(b2s + ks * 256, 128, sbo2), idesc2, ks > 0 ? 1u : 0u);
+        commit_one(bar(BAR_S2DONE + (j & 1)));
+      }
     }
-    if (lane == 0 && *abort) {  // drain this thread's tensor-core work
-      umma_commit(bar(BAR_DRAIN));
-      mbar_drain(bar(BAR_DRAIN), 0);
+    if (*abort) {  // drain this warp's tensor-core work
+      commit_one(bar(BAR_DRAIN));
+      if (lane == 0) mbar_drain(bar(BAR_DRAIN), 0);
     }
     __syncwarp();
   } else if (warp == 13) {
     // ===================== issuer B: S3 of each piece (and S1, shared buffers) ================
     bool ok = true;
+    const uint32_t sbo3 = (uint32_t)(K3 / 8) * 128;
+    const uint32_t idesc3 = umma_idesc<__half>(128, p.N3P);
     for (int j = 0; j < np; ++j) {
-      named_sync(kBarC2Done + (j & 1), 128 + 32);  // C2(j): all of D2(j) read, A3(j) written
-      if (lane == 0 && ok && !*abort) {
-        tc_fence_after();
-        ok = p.b3_all ? mbar_wait(bar(BAR_B3FULL), 0, abort)
-                      : mbar_wait(bar(BAR_B3FULL + (j & 3)), (j >> 2) & 1, abort);
-        if (ok) {
-          tc_fence_after();
-          const uint32_t a3 = a3s + (j % p.NA3) * p.a3_bytes;
-          const uint32_t b3 = b3s + (p.b3_all ? j : (j & 3)) * p.b3_bytes;
-          const uint32_t sbo3 = (uint32_t)(K3 / 8) * 128;
-          const uint32_t idesc3 = umma_idesc<__half>(128, p.N3P);
-          for (int o = 0; o < o2n; ++o)
-            umma(tmem + p.d3_col + o * p.N3P, desc_plain(a3 + o * a3_block, 128, sbo3),
-                 desc_plain(b3, 128, sbo3), idesc3, j > 0 ? 1u : 0u);
-          umma_commit(bar(BAR_S3DONE + (j & 3)));
-          if (j == np - 1) umma_commit(bar(BAR_D3DONE));
-        }
-        // S1(j + 2) into the buffer that held D2(j) (shared arrangement)
-        if (ok && p.shared_d12 && j + 2 < np) ok = issue_s1(j + 2);
+      // ---- S1(j + 2) into the buffer whose D2(j) C2 has just read (shared arrangement)
+      if (ok && p.shared_d12 && j + 2 < np) {
+        ok = warp_wait(bar(BAR_D2READ + (j & 1)), (j >> 1) & 1, abort);
+        if (ok) ok = issue_s1(j + 2);
       }
-      __syncwarp();
+      // ---- S3(j): C2(j) wrote A3(j); B3 landed
+      if (ok) ok = warp_wait(bar(BAR_C2DONE + (j & 1)), (j >> 1) & 1, abort);
+      if (ok)
+        ok = p.b3_all ? warp_wait(bar(BAR_B3FULL), 0, abort)
+                      : warp_wait(bar(BAR_B3FULL + j % p.NB3), (j / p.NB3) & 1, abort);
+      if (ok) {
+        const uint32_t a3 = a3s + (j % p.NA3) * p.a3_bytes;
+        const uint32_t b3 = b3s + (p.b3_all ? j : j % p.NB3) * p.b3_bytes;
+        for (int o = 0; o < o2n; ++o)
+          umma_one(tmem + p.d3_col + o * p.N3P, desc_plain(a3 + o * a3_block, 128, sbo3),
+                   desc_plain(b3, 128, sbo3), idesc3, j > 0 ? 1u : 0u);
+        commit_one(bar(BAR_S3DONE + (j & 15)));
+        if (j == np - 1) commit_one(bar(BAR_D3DONE));
+      }
     }
-    if (lane == 0 && *abort) {  // drain this thread's tensor-core work
-      umma_commit(bar(BAR_DRAIN + 1));
-      mbar_drain(bar(BAR_DRAIN + 1), 0);
+    if (*abort) {  // drain this warp's tensor-core work
+      commit_one(bar(BAR_DRAIN + 1));
+      if (lane == 0) mbar_drain(bar(BAR_DRAIN + 1), 0);
     }
     __syncwarp();
   } else {
@@ -464,7 +490,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
       if (p.b3_all) {
         bulk_load(b3s, p.b3 + (size_t)pa * p.b3_bytes, np * p.b3_bytes, bar(BAR_B3FULL));
       } else {
-        for (int q = 0; q < 4 && q < np; ++q)
+        for (int q = 0; q < p.NB3 && q < np; ++q)
           bulk_load(b3s + q * p.b3_bytes, p.b3 + (size_t)(pa + q) * p.b3_bytes, p.b3_bytes,
                     bar(BAR_B3FULL + q));
       }
@@ -491,7 +517,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
         if (ok) ok = mbar_wait(bar(BAR_S1DONE + (j & 3)), (j >> 2) & 1, abort);
         if (ok && j >= p.NA2)  // S2 of the piece that last used this A2 buffer completed
           ok = mbar_wait(bar(BAR_S2DONE + ((j - p.NA2) & 1)), ((j - p.NA2) >> 1) & 1, abort);
-        tc_fence_after();
+        bool d1_read = false;
         if (ok) {
           unsigned char* a2 = smem + p.off_a2 + ab * p.a2_bytes;
           const uint32_t d1 = tmem + lane_base + d1_col(j);
@@ -501,6 +527,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
             for (int u = 0; u < OB; ++u)
               if (ob + u < o1b) tmem_ld<RP>(d1 + (ob + u) * RP, v[u]);
             tmem_wait_ld();
+            if (ob + OB >= o1b) {  // last read of D1(j): S1 of a later piece may overwrite it
+              __syncwarp();
+              if (lane == 0) mbar_arrive(bar(BAR_D1READ + (j & 1)));
+              d1_read = true;
+            }
             if (rvalid) {
 #pragma unroll
               for (int u = 0; u < OB; ++u) {
@@ -520,8 +551,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
           }
           fence_async_smem();
         }
-        tc_fence_before();
-        named_arrive(kBarC1Done + (j & 1), 256 + 32);  // hand piece j to issuer A
+        if (!d1_read) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(BAR_D1READ + (j & 1)));
+        }
+        __syncwarp();  // hand piece j to issuer A
+        if (lane == 0) mbar_arrive(bar(BAR_C1DONE + (j & 1)));
       }
     } else if (warp < 12) {
       // ============================ C2: D2 -> A3 ============================
@@ -531,25 +566,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
         const int db = j & 1, ab = j % p.NA3;
         if (ok) ok = mbar_wait(bar(BAR_S2DONE + db), (j >> 1) & 1, abort);
         if (ok && j >= p.NA3)  // S3 of the piece that last used this A3 buffer completed
-          ok = mbar_wait(bar(BAR_S3DONE + ((j - p.NA3) & 3)), ((j - p.NA3) >> 2) & 1, abort);
-        tc_fence_after();
+          ok = mbar_wait(bar(BAR_S3DONE + ((j - p.NA3) & 15)), ((j - p.NA3) >> 4) & 1, abort);
         if (ok) {
           const uint32_t d2 = tmem + lane_base + d2_col(j);
           unsigned char* rowp =
               smem + p.off_a3 + ab * p.a3_bytes + (r >> 3) * ((K3 / 8) * 128) + (r & 7) * 16;
-          for (int c0 = 0; c0 < p.N2; c0 += 64) {
-            uint32_t v[4][16];
+          for (int c0 = 0; c0 < p.N2; c0 += 16 * CB) {
+            uint32_t v[CB][16];
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
+            for (int c = 0; c < CB; ++c)
               if (c0 + c * 16 < p.N2) tmem_ld<16>(d2 + c0 + c * 16, v[c]);
             tmem_wait_ld();
-            if (!p.shared_d12 && c0 + 64 >= p.N2) {  // last read of D2: S2 may reuse the buffer
-              tc_fence_before();
+            if (c0 + 16 * CB >= p.N2) {  // last read of D2(j): its buffer may be reused
               __syncwarp();
-              if (lane == 0) mbar_arrive(bar(BAR_D2FREE + db));
+              if (lane == 0) mbar_arrive(bar(BAR_D2READ + db));
             }
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < CB; ++c) {
 #pragma unroll
               for (int hh = 0; hh < 2; ++hh) {
                 const int col = c0 + c * 16 + 8 * hh;  // D2 column = o * RP + v
@@ -562,17 +595,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
             }
           }
           fence_async_smem();
-        } else if (!p.shared_d12) {
+        } else {
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar(BAR_D2FREE + db));
+          if (lane == 0) mbar_arrive(bar(BAR_D2READ + db));
         }
-        tc_fence_before();
-        named_arrive(kBarC2Done + (j & 1), 128 + 32);  // hand piece j to issuer B
+        __syncwarp();  // hand piece j to issuer B
+        if (lane == 0) mbar_arrive(bar(BAR_C2DONE + (j & 1)));
       }
     } else {
       // ==================== feeder: ring refills and the x slices of further i3 ================
       // Polls; every decision is taken by all lanes together (a vote over their own tests).
-      int r1 = p.b1_all ? np : min(NB1, np), r3 = p.b3_all ? np : min(4, np), q = 2;
+      int r1 = p.b1_all ? np : min(NB1, np), r3 = p.b3_all ? np : min(p.NB3, np), q = 2;
       unsigned idle = 0;
       while ((q < nq || r1 < np || r3 < np) && !*abort) {
         bool prog = false;
@@ -595,11 +628,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
           ++r1;
           prog = true;
         }
-        if (r3 < np && __all_sync(0xffffffffu, mbar_test(bar(BAR_S3DONE + ((r3 - 4) & 3)),
-                                                         ((r3 - 4) >> 2) & 1))) {
+        if (r3 < np &&
+            __all_sync(0xffffffffu, mbar_test(bar(BAR_S3DONE + ((r3 - p.NB3) & 15)),
+                                              ((r3 - p.NB3) >> 4) & 1))) {
           if (lane == 0)
-            bulk_load(b3s + (r3 & 3) * p.b3_bytes, p.b3 + (size_t)(pa + r3) * p.b3_bytes,
-                      p.b3_bytes, bar(BAR_B3FULL + (r3 & 3)));
+            bulk_load(b3s + (r3 % p.NB3) * p.b3_bytes, p.b3 + (size_t)(pa + r3) * p.b3_bytes,
+                      p.b3_bytes, bar(BAR_B3FULL + r3 % p.NB3));
           __syncwarp();
           ++r3;
           prog = true;
@@ -621,8 +655,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
             mbar_drain(bar(BAR_G1FULL + k % NB1), (k / NB1) & 1);
         if (p.b3_all) mbar_drain(bar(BAR_B3FULL), 0);
         else
-          for (int k = max(0, r3 - 4); k < r3; ++k)
-            mbar_drain(bar(BAR_B3FULL + (k & 3)), (k >> 2) & 1);
+          for (int k = max(0, r3 - p.NB3); k < r3; ++k)
+            mbar_drain(bar(BAR_B3FULL + k % p.NB3), (k / p.NB3) & 1);
       }
       __syncwarp();
     }
@@ -638,29 +672,49 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
     tc_fence_after();
     const int r = 32 * (warp & 3) + lane;
     const bool vec4 = (sh.O3 & 3) == 0;
+    const int nc16 = p.N3P / 16;
     for (int o = warp >> 2; o < o2n; o += 3) {
-      for (int c16 = 0; c16 < p.N3P / 16; ++c16) {
-        uint32_t v[16];
+      // all of this o's TMEM chunks in flight at once, one wait
+      uint32_t v[4][16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (c < nc16 && ok) {
+          tmem_ld<16>(tmem + lane_base + p.d3_col + o * p.N3P + c * 16, v[c]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[c][i] = 0u;
+        }
+      }
+      if (ok) tmem_wait_ld();
+      for (int c16 = 4; c16 < nc16; ++c16) {  // o3 beyond 64: one chunk at a time
+        uint32_t w[16];
         if (ok) {
-          tmem_ld<16>(tmem + lane_base + p.d3_col + o * p.N3P + c16 * 16, v);
+          tmem_ld<16>(tmem + lane_base + p.d3_col + o * p.N3P + c16 * 16, w);
           tmem_wait_ld();
         } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = 0u;
+          for (int i = 0; i < 16; ++i) w[i] = 0u;
         }
-        if (r < rows) {
-          float* dst = ys + r * ystr + o * sh.O3 + c16 * 16;
+        if (r < rows)
+          for (int i = 0; i < 16; ++i)
+            if (c16 * 16 + i < sh.O3) ys[r * ystr + o * sh.O3 + c16 * 16 + i] = __uint_as_float(w[i]);
+      }
+      if (r < rows) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (c >= nc16) break;
+          float* dst = ys + r * ystr + o * sh.O3 + c * 16;
           if (vec4) {
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              if (c16 * 16 + 4 * k < sh.O3)
+              if (c * 16 + 4 * k < sh.O3)
                 *reinterpret_cast<float4*>(dst + 4 * k) =
-                    make_float4(__uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
-                                __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3]));
+                    make_float4(__uint_as_float(v[c][4 * k]), __uint_as_float(v[c][4 * k + 1]),
+                                __uint_as_float(v[c][4 * k + 2]), __uint_as_float(v[c][4 * k + 3]));
           } else {
 #pragma unroll
             for (int i = 0; i < 16; ++i)
-              if (c16 * 16 + i < sh.O3) dst[i] = __uint_as_float(v[i]);
+              if (c * 16 + i < sh.O3) dst[i] = __uint_as_float(v[c][i]);
           }
         }
       }
@@ -676,118 +730,116 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   }
   if (tid == 0 && *abort) atomicExch(p.status, (int)TR_ERR_TIMEOUT);
 
-  // ---- reduce over the cluster: each CTA sums its slice of the tile from every peer's partial
-  // (distributed shared memory, rank order), then across clusters through workspace slots
-  if (p.CL > 1) cluster.sync();  // all peers' partials are in their shared memory
-  auto peer = [&](int k) -> const float* { return p.CL > 1 ? cluster.map_shared_rank(ys, k) : ys; };
+  // ---- reduce over the cluster.  Items: 8 consecutive o3 (vector path) or single elements.
+  // Item e of the tile is owned by cluster rank e / SL.  Every CTA pushes each of its partial
+  // items into the owner's receive buffer (recv[sender rank][item], distributed shared-memory
+  // stores, no waiting); after the next cluster barrier each owner adds its items' CL partials from
+  // its own shared memory in rank order, then writes y (one cluster per tile) or its workspace
+  // slot (NC > 1; the last cluster to finish adds the NC slots in cluster order).
+  const int W = p.vec_out ? 8 : 1;  // floats per item
+  const int nper = p.vec_out ? sh.O3 / 8 : sh.O3;
+  const int nout = rows * o2n * nper;
+  const int SL = (nout + p.CL - 1) / p.CL;
+  const int ebeg = crank * SL, eend = min(nout, ebeg + SL);
+  float* recv = ys + p.recv_off;
+  auto item_idx = [&](int e) {  // offset of item e inside ys
+    const int o3v = e % nper, q = e / nper;
+    return (q / o2n) * ystr + (q % o2n) * sh.O3 + o3v * W;
+  };
+  if (p.CL > 1) {
+    // the receive buffers overlap the peers' operand space: every CTA of the cluster must be
+    // past its piece loop (and have its partial in shared memory) before anyone pushes
+    cluster.sync();
+    for (int e = tid; e < nout; e += kTcThreads) {
+      const int owner = e / SL, li = e - owner * SL;
+      float* dst = cluster.map_shared_rank(recv, owner) + ((size_t)crank * SL + li) * W;
+      const float* src = ys + item_idx(e);
+      if (p.vec_out) {
+        reinterpret_cast<float4*>(dst)[0] = reinterpret_cast<const float4*>(src)[0];
+        reinterpret_cast<float4*>(dst)[1] = reinterpret_cast<const float4*>(src)[1];
+      } else {
+        *dst = *src;
+      }
+    }
+    cluster.sync();  // every push landed; nobody touches a peer's shared memory after this
+  }
   E* y = static_cast<E*>(p.y) + (size_t)t0 * sh.d_out;
   float* slot = p.NC > 1
       ? p.slots + (((size_t)tile * p.NG + grp) * p.NC + cl_id) * (size_t)p.slot_elems
       : nullptr;
   const float* s0 = p.slots + ((size_t)tile * p.NG + grp) * p.NC * (size_t)p.slot_elems;
-  if (p.vec_out) {
-    // 8 consecutive o3 per item: two float4 per partial, one 16-byte store of y
-    const int nv3 = sh.O3 / 8;
-    const int nout = rows * o2n * nv3;
-    const int SL = (nout + p.CL - 1) / p.CL;
-    const int ebeg = crank * SL, eend = min(nout, ebeg + SL);
-    for (int e = ebeg + tid; e < eend; e += kTcThreads) {
-      const int o3v = e % nv3, q = e / nv3;
-      const int o = q % o2n, r = q / o2n;
-      const int idx = r * ystr + o * sh.O3 + o3v * 8;
-      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+  // write the 8 (or 1) finished values of item e to y
+  auto store_y = [&](int e, const float* f) {
+    const int o3v = e % nper, q = e / nper;
+    const int o = q % o2n, r = q / o2n;
+    const int t = r / sh.O1, o1 = r - t * sh.O1;
+    E* dst = y + (size_t)t * sh.d_out + o1 * sh.sy1 + (o2a + o) * sh.sy2 + o3v * W * sh.sy3;
+    if (p.vec_out) {
+      uint4 out;
+      out.x = pack2<E>(f[0], f[1]);
+      out.y = pack2<E>(f[2], f[3]);
+      out.z = pack2<E>(f[4], f[5]);
+      out.w = pack2<E>(f[6], f[7]);
+      *reinterpret_cast<uint4*>(dst) = out;
+    } else {
+      *dst = from_f32<E>(f[0]);
+    }
+  };
+  for (int e = ebeg + tid; e < eend; e += kTcThreads) {
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (p.CL > 1) {
+      const float* src = recv + (size_t)(e - ebeg) * W;
       for (int k = 0; k < p.CL; ++k) {
-        const float* pk = peer(k);
-        const float4 u = *reinterpret_cast<const float4*>(pk + idx);
-        const float4 w = *reinterpret_cast<const float4*>(pk + idx + 4);
-        a.x += u.x; a.y += u.y; a.z += u.z; a.w += u.w;
-        b.x += w.x; b.y += w.y; b.z += w.z; b.w += w.w;
+        const float* rk = src + (size_t)k * SL * W;
+        if (p.vec_out) {
+          const float4 u = reinterpret_cast<const float4*>(rk)[0];
+          const float4 w = reinterpret_cast<const float4*>(rk)[1];
+          f[0] += u.x; f[1] += u.y; f[2] += u.z; f[3] += u.w;
+          f[4] += w.x; f[5] += w.y; f[6] += w.z; f[7] += w.w;
+        } else {
+          f[0] += rk[0];
+        }
       }
-      if (p.NC > 1) {
-        float4* d = reinterpret_cast<float4*>(slot + (size_t)(r * o2n + o) * sh.O3 + o3v * 8);
-        d[0] = a;
-        d[1] = b;
-      } else {
-        const int t = r / sh.O1, o1 = r - t * sh.O1;
-        uint4 out;
-        out.x = pack2<E>(a.x, a.y);
-        out.y = pack2<E>(a.z, a.w);
-        out.z = pack2<E>(b.x, b.y);
-        out.w = pack2<E>(b.z, b.w);
-        *reinterpret_cast<uint4*>(y + (size_t)t * sh.d_out + o1 * sh.sy1 + (o2a + o) * sh.sy2 +
-                                  o3v * 8) = out;
-      }
+    } else {
+      const float* src = ys + item_idx(e);
+      for (int i = 0; i < W; ++i) f[i] = src[i];
     }
-    if (p.CL > 1) cluster.sync();  // peers finished reading this CTA's shared memory
     if (p.NC > 1) {
+      float* d = slot + (size_t)e * W;
+      if (p.vec_out) {
+        reinterpret_cast<float4*>(d)[0] = make_float4(f[0], f[1], f[2], f[3]);
+        reinterpret_cast<float4*>(d)[1] = make_float4(f[4], f[5], f[6], f[7]);
+      } else {
+        *d = f[0];
+      }
+    } else {
+      store_y(e, f);
+    }
+  }
+  if (p.NC > 1) {
+    __threadfence();
+    __syncthreads();
+    int* counter = p.cnt + ((size_t)tile * p.NG + grp) * p.CL + crank;
+    if (tid == 0) *flag = (atomicAdd(counter, 1) == p.NC - 1);
+    __syncthreads();
+    if (*flag) {  // last cluster for this slice: add the NC slots in cluster order, write y
       __threadfence();
-      __syncthreads();
-      int* counter = p.cnt + ((size_t)tile * p.NG + grp) * p.CL + crank;
-      if (tid == 0) *flag = (atomicAdd(counter, 1) == p.NC - 1);
-      __syncthreads();
-      if (*flag) {  // last cluster for this slice: add the NC slots in cluster order, write y
-        __threadfence();
-        for (int e = ebeg + tid; e < eend; e += kTcThreads) {
-          const int o3v = e % nv3, q = e / nv3;
-          const int o = q % o2n, r = q / o2n;
-          const size_t off = (size_t)(r * o2n + o) * sh.O3 + o3v * 8;
-          float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
-          for (int c = 0; c < p.NC; ++c) {
-            const float4 u = __ldcg(reinterpret_cast<const float4*>(s0 + (size_t)c * p.slot_elems + off));
-            const float4 w = __ldcg(reinterpret_cast<const float4*>(s0 + (size_t)c * p.slot_elems + off + 4));
-            a.x += u.x; a.y += u.y; a.z += u.z; a.w += u.w;
-            b.x += w.x; b.y += w.y; b.z += w.z; b.w += w.w;
+      for (int e = ebeg + tid; e < eend; e += kTcThreads) {
+        float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int c = 0; c < p.NC; ++c) {
+          const float* sc = s0 + (size_t)c * p.slot_elems + (size_t)e * W;
+          if (p.vec_out) {
+            const float4 u = __ldcg(reinterpret_cast<const float4*>(sc));
+            const float4 w = __ldcg(reinterpret_cast<const float4*>(sc) + 1);
+            f[0] += u.x; f[1] += u.y; f[2] += u.z; f[3] += u.w;
+            f[4] += w.x; f[5] += w.y; f[6] += w.z; f[7] += w.w;
+          } else {
+            f[0] += __ldcg(sc);
           }
-          const int t = r / sh.O1, o1 = r - t * sh.O1;
-          uint4 out;
-          out.x = pack2<E>(a.x, a.y);
-          out.y = pack2<E>(a.z, a.w);
-          out.z = pack2<E>(b.x, b.y);
-          out.w = pack2<E>(b.z, b.w);
-          *reinterpret_cast<uint4*>(y + (size_t)t * sh.d_out + o1 * sh.sy1 + (o2a + o) * sh.sy2 +
-                                    o3v * 8) = out;
         }
-        if (tid == 0) atomicExch(counter, 0);
+        store_y(e, f);
       }
-    }
-  } else {
-    const int nout = rows * o2n * sh.O3;
-    const int SL = (nout + p.CL - 1) / p.CL;
-    const int ebeg = crank * SL, eend = min(nout, ebeg + SL);
-    for (int e = ebeg + tid; e < eend; e += kTcThreads) {
-      const int o3 = e % sh.O3, q = e / sh.O3;
-      const int o = q % o2n, r = q / o2n;
-      const int idx = r * ystr + o * sh.O3 + o3;
-      float sum = 0.f;
-      for (int k = 0; k < p.CL; ++k) sum += peer(k)[idx];
-      if (p.NC > 1) {
-        slot[e] = sum;
-      } else {
-        const int t = r / sh.O1, o1 = r - t * sh.O1;
-        y[(size_t)t * sh.d_out + o1 * sh.sy1 + (o2a + o) * sh.sy2 + o3 * sh.sy3] =
-            from_f32<E>(sum);
-      }
-    }
-    if (p.CL > 1) cluster.sync();  // peers finished reading this CTA's shared memory
-    if (p.NC > 1) {
-      __threadfence();
-      __syncthreads();
-      int* counter = p.cnt + ((size_t)tile * p.NG + grp) * p.CL + crank;
-      if (tid == 0) *flag = (atomicAdd(counter, 1) == p.NC - 1);
-      __syncthreads();
-      if (*flag) {  // last cluster for this slice: add the NC slots in cluster order, write y
-        __threadfence();
-        for (int e = ebeg + tid; e < eend; e += kTcThreads) {
-          float sum = 0.f;
-          for (int c = 0; c < p.NC; ++c) sum += __ldcg(s0 + (size_t)c * p.slot_elems + e);
-          const int o3 = e % sh.O3, q = e / sh.O3;
-          const int o = q % o2n, r = q / o2n;
-          const int t = r / sh.O1, o1 = r - t * sh.O1;
-          y[(size_t)t * sh.d_out + o1 * sh.sy1 + (o2a + o) * sh.sy2 + o3 * sh.sy3] =
-              from_f32<E>(sum);
-        }
-        if (tid == 0) atomicExch(counter, 0);
-      }
+      if (tid == 0) atomicExch(counter, 0);
     }
   }
 }
@@ -873,6 +925,7 @@ static void fill_tc(TcParams<S>& tp, const Plan& p, const TcGeom& g, const void*
   tp.a3_bytes = (int)g.a3_bytes;
   tp.a1_bytes = (int)g.a1_bytes;
   tp.ystr = g.ystr;
+  tp.recv_off = 128 * g.ystr;  // floats: the receive buffers follow the partial y
   const Canon& c = p.c;
   tp.vec_out = c.sy3 == 1 && c.O3 % 8 == 0 && c.sy1 % 8 == 0 && c.sy2 % 8 == 0 &&
                c.d_out % 8 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;

@@ -295,8 +295,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   const S& sh = p.sh;
   constexpr int K3 = 16;         // S3 K (v padded to 16)
   constexpr int NCH = RP / 8;    // 16-byte chunks of one (o1 or o2, i2) run of RP values
-  constexpr int OB = RP == 16 ? 5 : 8;  // o1 per TMEM batch in C1 (<= 80 columns, one wait)
-  constexpr int CB = 5;          // 16-column chunks per TMEM batch in C2
+  constexpr int CB = 5;          // 16-column TMEM loads per wait in C1 and C2 (80 columns)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -521,29 +520,40 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
         if (ok) {
           unsigned char* a2 = smem + p.off_a2 + ab * p.a2_bytes;
           const uint32_t d1 = tmem + lane_base + d1_col(j);
-          for (int ob = o1a; ob < o1b; ob += OB) {
-            uint32_t v[OB][RP];
+          // D1 columns (o1, u) of this warp's o1 half, 16 per TMEM load, up to 80 per wait;
+          // a load may run past the half (never past the allocation): those columns are unused
+          const int cb0 = o1a * RP, ce = o1b * RP;
+          for (int cb = cb0; cb < ce; cb += 16 * CB) {
+            uint32_t v[CB][16];
 #pragma unroll
-            for (int u = 0; u < OB; ++u)
-              if (ob + u < o1b) tmem_ld<RP>(d1 + (ob + u) * RP, v[u]);
+            for (int c = 0; c < CB; ++c)
+              if (cb + 16 * c < ce) tmem_ld<16>(d1 + cb + 16 * c, v[c]);
             tmem_wait_ld();
-            if (ob + OB >= o1b) {  // last read of D1(j): S1 of a later piece may overwrite it
+            if (cb + 16 * CB >= ce) {  // last read of D1(j): S1 of a later piece may overwrite it
               __syncwarp();
               if (lane == 0) mbar_arrive(bar(BAR_D1READ + (j & 1)));
               d1_read = true;
             }
             if (rvalid) {
 #pragma unroll
-              for (int u = 0; u < OB; ++u) {
-                if (ob + u < o1b) {
-                  const int row = tq * sh.O1 + ob + u;
-                  if (NCH == 1) {
-                    *reinterpret_cast<uint4*>(a2 + a2_offset(row, i2)) = chunk_f16(v[u]);
-                  } else {
-                    const uint4 c0 = chunk_f16(v[u]), c1 = chunk_f16(v[u] + 8);
-                    *reinterpret_cast<uint4*>(a2 + a2_offset(row, 2 * i2 + rot)) = rot ? c1 : c0;
+              for (int c = 0; c < CB; ++c) {
+                const int col = cb + 16 * c;
+                if (NCH == 2) {  // RP 16: one load = one o1, two 16-byte chunks (u 0-7, 8-15);
+                  // lanes alternate which chunk they store first (bank spread)
+                  if (col < ce) {
+                    const int row = tq * sh.O1 + (col >> 4);
+                    const uint4 q0 = chunk_f16(v[c]), q1 = chunk_f16(v[c] + 8);
+                    *reinterpret_cast<uint4*>(a2 + a2_offset(row, 2 * i2 + rot)) = rot ? q1 : q0;
                     *reinterpret_cast<uint4*>(a2 + a2_offset(row, 2 * i2 + (rot ^ 1))) =
-                        rot ? c0 : c1;
+                        rot ? q0 : q1;
+                  }
+                } else {  // RP 8: one load = two o1, one 16-byte chunk each
+#pragma unroll
+                  for (int hh = 0; hh < 2; ++hh) {
+                    if (col + 8 * hh < ce) {
+                      const int row = tq * sh.O1 + ((col >> 3) + hh);
+                      *reinterpret_cast<uint4*>(a2 + a2_offset(row, i2)) = chunk_f16(v[c] + 8 * hh);
+                    }
                   }
                 }
               }

@@ -83,6 +83,15 @@ class Clocks:
         except OSError:
             self.proc = None
 
+    def wait_first_sample(self, timeout_s: float = 5.0) -> None:
+        """nvidia-smi needs a moment to start: block until it has written a line."""
+        t_end = time.perf_counter() + timeout_s
+        while self.proc is not None and time.perf_counter() < t_end:
+            self.file.flush()
+            if os.path.getsize(self.file.name) > 0:
+                return
+            time.sleep(0.05)
+
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
@@ -325,6 +334,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     clocks = Clocks(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ
                     else int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank]))
+    clocks.wait_first_sample()
     launches = 0
     for key, c in cases.items():
         c["cold"] = cold_device_us(c["fn"], c["x"], flush, steps, warmup)
@@ -332,7 +342,6 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    clk = clocks.stop()
 
     for key, c in cases.items():
         c["warm"] = warm_stream_us(c["fn"], c["x"])
@@ -355,6 +364,7 @@ def run_ours(args, rank, world, local_rank):
 
     prefill = (prefill_leg(args, rank, world, dev, tc_peak) if args.prefill_tokens > 0
                else None)
+    clk = clocks.stop()  # sampled from before the cold legs to the end of the prefill leg
     keys = list(cases)
     med = max_over_ranks([statistics.median(cases[k]["cold"]) for k in keys], world)
     mean = max_over_ranks([statistics.mean(cases[k]["cold"]) for k in keys], world)

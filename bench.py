@@ -13,6 +13,9 @@ Per case:
   e2e leg     the public API end to end: pinned host x -> device, fn(x), y -> pinned host,
               after an L2 flush and with the GPU idle, so host dispatch is inside the region.
   dense bar   F.linear(x, W) on the materialised fp16 W, same legs (TF32 off).
+Extra objects on the line: sharded_prefill (config 5, token-sharded over the ranks) and
+decode_chain (config 4: a T=1 decode step through several layers, fused consumers vs the
+reference's separate consumer launches vs dense bf16; see decode_chain_leg).
 value = mean over the five cases of the mean value-leg time (the device timer on this part ticks
 in ~2 us steps, so single-call medians are quantised; means over the steps are not).
 ms_per_step = one call of each case.  --impl reference times the reference's CPU path (the numpy restatement in oracle/) on the
@@ -52,6 +55,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-dense", action="store_true")
+    ap.add_argument("--chain-layers", type=int, default=4,
+                    help="layers of the config-4 decode chain leg (0 = skip)")
     ap.add_argument("--prefill-tokens", type=int, default=65536,
                     help="tokens of the sharded prefill leg (config 5), split over the ranks; "
                          "0 skips it")
@@ -305,6 +310,92 @@ def prefill_leg(args, rank, world, dev, tc_peak):
     return out
 
 
+def decode_chain_leg(dev, layers, T=1):
+    """Config 4: one decode step (T=1, bf16, R16) through `layers` transformer layers of TR
+    projections q, k, v, o, gate, up, down (distinct seeded cores per layer; 2.5 MB of packed
+    cores a layer, L2-resident when warm).  Attention is not simulated (o reads q's output, as
+    in the reference's chain, tools/qwen_model_chain.py:111-134).  Three orders, warm stream
+    (5 blocks x 10 steps, median), microseconds per layer:
+      fused      o/down with the residual add and up with silu(gate)*up in their own store,
+                 gate in fp32: 7 launches a layer;
+      unfused    the reference's order: accumulate (fp32) then consume_add / consume_silu_mul
+                 launches: 10 launches a layer;
+      dense      cuBLAS bf16 F.linear on dense weights of the same shapes (random values; the
+                 time does not depend on them) with torch's add / silu / mul.
+    The fused step is also captured in a CUDA graph and replayed."""
+    import torch.nn.functional as F
+
+    from kernel_task_b200 import consume_add, consume_silu_mul, prepare_optimized
+    from kernel_task_b200.spec import SPEC_C4, baseline_cores, baseline_x
+
+    names = ["q", "k", "v", "o", "gate", "up", "down"]
+    L = [{n: prepare_optimized(baseline_cores(SPEC_C4[n], seed=100 * l + i,
+                                              dtype=torch.bfloat16, device=dev), SPEC_C4[n])
+          for i, n in enumerate(names)} for l in range(layers)]
+    h0 = baseline_x(SPEC_C4["q"], T, seed=9, dtype=torch.bfloat16, device=dev)
+
+    def fused(h):
+        for ops in L:
+            q = ops["q"](h)
+            ops["k"](h)
+            ops["v"](h)
+            h = ops["o"].forward_add(q, h)
+            act = ops["up"].forward_silu_mul(h, ops["gate"].accumulate(h))
+            h = ops["down"].forward_add(act, h)
+        return h
+
+    def unfused(h):
+        for ops in L:
+            q = ops["q"](h)
+            ops["k"](h)
+            ops["v"](h)
+            h = consume_add(h, ops["o"].accumulate(q))
+            act = consume_silu_mul(ops["gate"].accumulate(h), ops["up"].accumulate(h))
+            h = consume_add(h, ops["down"].accumulate(act))
+        return h
+
+    g = torch.Generator(device=dev).manual_seed(1)
+    Ws = [{n: (torch.randn(SPEC_C4[n].out_features, SPEC_C4[n].in_features, generator=g,
+                           device=dev) * 0.01).to(torch.bfloat16) for n in names}
+          for _ in range(layers)]
+
+    def dense(h):
+        for W in Ws:
+            q = F.linear(h, W["q"])
+            F.linear(h, W["k"])
+            F.linear(h, W["v"])
+            h = h + F.linear(q, W["o"])
+            h = h + F.linear(F.silu(F.linear(h, W["gate"])) * F.linear(h, W["up"]), W["down"])
+        return h
+
+    out = {"workload": f"config 4 decode step, T={T}, bf16, R16, {layers} layers "
+                       "(q,k,v,o,gate,up,down; attention not simulated)",
+           "launches_per_layer": {"fused": 7, "unfused": 10}}
+    a, b = fused(h0), unfused(h0)
+    rel = ((a.float() - b.float()).norm() / b.float().norm()).item()
+    out["fused_vs_unfused_rel_frob"] = float(f"{rel:.3g}")
+    for name, fn in (("fused", fused), ("unfused", unfused), ("dense_bf16", dense)):
+        out[f"{name}_us_per_layer"] = round(warm_stream_us(fn, h0, 5, 10) / layers, 3)
+    try:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                fused(h0)
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fused(h0)
+        out["fused_graph_us_per_layer"] = round(
+            warm_stream_us(lambda _: graph.replay(), None, 5, 10) / layers, 3)
+        del graph
+    except RuntimeError as e:  # report, keep the rest of the line
+        out["fused_graph_error"] = str(e).splitlines()[0][:200]
+    del L, Ws
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, rank, world, local_rank):
     from kernel_task_b200 import prepare_optimized
     from kernel_task_b200.spec import TRSpec, baseline_cores, baseline_x
@@ -364,7 +455,9 @@ def run_ours(args, rank, world, local_rank):
 
     prefill = (prefill_leg(args, rank, world, dev, tc_peak) if args.prefill_tokens > 0
                else None)
-    clk = clocks.stop()  # sampled from before the cold legs to the end of the prefill leg
+    chain = (decode_chain_leg(dev, args.chain_layers)
+             if args.chain_layers > 0 and world == 1 else None)
+    clk = clocks.stop()  # sampled from before the cold legs to the end of the chain leg
     keys = list(cases)
     med = max_over_ranks([statistics.median(cases[k]["cold"]) for k in keys], world)
     mean = max_over_ranks([statistics.mean(cases[k]["cold"]) for k in keys], world)
@@ -423,6 +516,8 @@ def run_ours(args, rank, world, local_rank):
     }
     if prefill is not None:
         line["sharded_prefill"] = prefill
+    if chain is not None:
+        line["decode_chain"] = chain
     if world == 1:
         value_cpu, threads, cpu_cases = cpu_reference_leg(1.0)
         line["cpu_baseline"] = {"value": round(value_cpu, 2), "unit": "us/call", "cores": threads,

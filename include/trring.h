@@ -25,6 +25,11 @@
  *   tr_workspace_bytes               <- the design-B workspace sizing in PreparedTRKernel.__call__
  *                                       (tr_kernel.py:290-296, 314-317)
  *   tr_plan_destroy                  <- releasing the PreparedTRKernel (Python GC in the reference)
+ *   tr_forward_epilogue              <- PreparedTRKernel.accumulate (tr_kernel.py:230-243) and
+ *                                       the extension's forward_fp32 (csrc/v3g/bind.cu:84-91),
+ *                                       with the consumers below fused into the same launch
+ *   tr_consume_silu_mul              <- consume_silu_mul (csrc/v3g/bind.cu:93-108, 123-133)
+ *   tr_consume_add                   <- consume_add (csrc/v3g/bind.cu:110-121, 135-148)
  */
 #ifndef TRRING_H
 #define TRRING_H
@@ -124,6 +129,38 @@ int tr_forward_tiled(const tr_plan* plan, const void* packed, const void* x, int
 #define TR_NOALLOC_SCRATCH_BYTES (8u << 20)
 int tr_forward_noalloc(const tr_plan* plan, const void* packed, const void* x, int64_t tokens,
                        void* y, void* stream);
+
+/* Epilogues applied to each finished y element v inside the forward kernel, before the one
+ * store of y (no extra launch, no fp32 round trip through memory):
+ *   TR_EPI_NONE      y = v
+ *   TR_EPI_ADD       y = aux + v            (residual add after a projection)
+ *   TR_EPI_SILU_MUL  y = silu(aux) * v      (gated MLP: aux = gate(x), v = up(x))
+ * aux is [tokens, d_out] row-major, fp32 or the plan's dtype, 16-byte aligned; it may be y
+ * itself (an in-place residual add) but must not overlap y otherwise, nor x.  out_dtype is
+ * TR_F32 (y stored as fp32: the reference's accumulate / forward_fp32) or the plan's dtype.
+ * The arithmetic is fp32: v + aux, and aux / (1 + exp(-aux)) * v, rounded once on store.   */
+enum tr_epilogue_kind { TR_EPI_NONE = 0, TR_EPI_ADD = 1, TR_EPI_SILU_MUL = 2 };
+typedef struct tr_epilogue {
+  int32_t kind;      /* tr_epilogue_kind                          */
+  int32_t out_dtype; /* TR_F32 or the plan's dtype                */
+  const void* aux;   /* second operand (unused for TR_EPI_NONE)   */
+  int32_t aux_dtype; /* TR_F32 or the plan's dtype                */
+} tr_epilogue;
+
+/* tr_forward_tiled with an epilogue (NULL epilogue = plain forward in the plan's dtype). */
+int tr_forward_epilogue(const tr_plan* plan, const void* packed, const void* x, int64_t tokens,
+                        void* y, const tr_epilogue* epilogue, void* workspace,
+                        size_t workspace_bytes, const tr_tiling* tiling, void* stream);
+
+/* The reference's stand-alone consumers of fp32 forward outputs, for callers that keep the
+ * unfused order.  n elements, n % 4 == 0, all pointers 16-byte aligned, out_dtype TR_F16 or
+ * TR_BF16.  Like the reference, each clears (zero-fills) the fp32 inputs it consumed.
+ *   tr_consume_silu_mul: out = silu(g) * u;  g, u fp32, both cleared
+ *   tr_consume_add:      out = h + y;        h in out_dtype, y fp32, y cleared             */
+int tr_consume_silu_mul(float* g, float* u, void* out, int32_t out_dtype, int64_t n,
+                        void* stream);
+int tr_consume_add(const void* h, float* y, void* out, int32_t out_dtype, int64_t n,
+                   void* stream);
 
 /* The geometry tr_forward would use for `tokens` (after clamping to this device). */
 int tr_plan_tiling(const tr_plan* plan, int64_t tokens, tr_tiling* out);

@@ -13,10 +13,10 @@ thin PyTorch binding used here.
 """
 from .spec import (SPEC_C1, SPEC_C2, SPEC_C3, SPEC_C4, SPEC_C5, TRSpec, baseline_cores,
                    baseline_sigma, baseline_x, make_cores, validate, validate_cores)
-from .ring import prepare_optimized, tr_forward_optimized
+from .ring import consume_add, consume_silu_mul, prepare_optimized, tr_forward_optimized
 
 __all__ = [
     "TRSpec", "make_cores", "baseline_cores", "baseline_sigma", "baseline_x", "validate",
-    "validate_cores", "prepare_optimized", "tr_forward_optimized",
+    "validate_cores", "prepare_optimized", "tr_forward_optimized", "consume_silu_mul", "consume_add",
     "SPEC_C1", "SPEC_C2", "SPEC_C3", "SPEC_C4", "SPEC_C5",
 ]

@@ -17,6 +17,7 @@ TR_ERR_ALIGN = -5
 TR_ERR_TIMEOUT = -6
 TR_F32, TR_F16, TR_BF16 = 0, 1, 2
 KERNEL_AUTO, KERNEL_GENERIC, KERNEL_MMA, KERNEL_TC05, KERNEL_DECODE = 0, 1, 2, 3, 4
+TR_EPI_NONE, TR_EPI_ADD, TR_EPI_SILU_MUL = 0, 1, 2
 
 
 class TrSpec(ctypes.Structure):
@@ -26,6 +27,11 @@ class TrSpec(ctypes.Structure):
 class TrTiling(ctypes.Structure):
     _fields_ = [("tokens_per_tile", c_int32), ("cluster", c_int32), ("clusters", c_int32),
                 ("kernel", c_int32)]
+
+
+class TrEpilogue(ctypes.Structure):
+    _fields_ = [("kind", c_int32), ("out_dtype", c_int32), ("aux", c_void_p),
+                ("aux_dtype", c_int32)]
 
 
 # name -> (restype, argtypes); every function declared in include/trring.h
@@ -43,6 +49,11 @@ PROTOTYPES = {
     "tr_forward_tiled": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
                                  c_size_t, POINTER(TrTiling), c_void_p]),
     "tr_forward_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
+    "tr_forward_epilogue": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
+                                    POINTER(TrEpilogue), c_void_p, c_size_t, POINTER(TrTiling),
+                                    c_void_p]),
+    "tr_consume_silu_mul": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int64, c_void_p]),
+    "tr_consume_add": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int64, c_void_p]),
     "tr_plan_tiling": (c_int, [c_void_p, c_int64, POINTER(TrTiling)]),
     "tr_plan_describe": (c_int, [c_void_p, c_char_p, c_size_t]),
     "tr_plan_flops_per_token": (c_int, [c_void_p, POINTER(c_double)]),
@@ -124,6 +135,14 @@ class Plan:
         """tr_forward with the library's built-in scratch (no caller workspace)."""
         return lib().tr_forward_noalloc(self.handle, c_void_p(packed_ptr), c_void_p(x_ptr),
                                         tokens, c_void_p(y_ptr), c_void_p(stream))
+
+    def forward_epilogue(self, packed_ptr: int, x_ptr: int, tokens: int, y_ptr: int,
+                         epilogue: TrEpilogue | None, ws_ptr: int = 0, ws_bytes: int = 0,
+                         stream: int = 0, tiling: TrTiling | None = None) -> int:
+        return lib().tr_forward_epilogue(
+            self.handle, c_void_p(packed_ptr), c_void_p(x_ptr), tokens, c_void_p(y_ptr),
+            ctypes.byref(epilogue) if epilogue else None, c_void_p(ws_ptr or None), ws_bytes,
+            ctypes.byref(tiling) if tiling else None, c_void_p(stream))
 
     def tiling(self, tokens: int) -> TrTiling:
         t = TrTiling()

@@ -43,6 +43,58 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
 }
+// packed 16-bit pair -> two floats (x = low half)
+template <typename E>
+__device__ __forceinline__ float2 unpack2(uint32_t w);
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t w) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+}
+
+// ---- output epilogue (struct Epi, plan.h): the value written for y[i], and the store
+template <typename E, class EP>
+__device__ __forceinline__ float epi_value(const EP& ep, size_t i, float v) {
+  if (ep.kind == 0) return v;
+  const float a = ep.aux_f32 ? static_cast<const float*>(ep.aux)[i]
+                             : to_f32<E>(static_cast<const E*>(ep.aux)[i]);
+  if (ep.kind == 1) return a + v;
+  return a / (1.f + __expf(-a)) * v;  // silu(a) * v
+}
+template <typename E, class EP>
+__device__ __forceinline__ void epi_store(const EP& ep, void* y, size_t i, float v) {
+  const float r = epi_value<E>(ep, i, v);
+  if (ep.out_f32) static_cast<float*>(y)[i] = r;
+  else static_cast<E*>(y)[i] = from_f32<E>(r);
+}
+// N consecutive elements y[i .. i + N - 1] (N = 4 or 8; 8-byte or 16-byte aligned in E, twice
+// that in fp32)
+template <typename E, int N, class EP>
+__device__ __forceinline__ void epi_store_vec(const EP& ep, void* y, size_t i, const float* f) {
+  float r[N];
+#pragma unroll
+  for (int k = 0; k < N; ++k) r[k] = epi_value<E>(ep, i + k, f[k]);
+  if (ep.out_f32) {
+    float4* d = reinterpret_cast<float4*>(static_cast<float*>(y) + i);
+#pragma unroll
+    for (int k = 0; k < N / 4; ++k) d[k] = make_float4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]);
+  } else if constexpr (N == 8) {
+    uint4 o;
+    o.x = pack2<E>(r[0], r[1]);
+    o.y = pack2<E>(r[2], r[3]);
+    o.z = pack2<E>(r[4], r[5]);
+    o.w = pack2<E>(r[6], r[7]);
+    *reinterpret_cast<uint4*>(static_cast<E*>(y) + i) = o;
+  } else {
+    uint2 o;
+    o.x = pack2<E>(r[0], r[1]);
+    o.y = pack2<E>(r[2], r[3]);
+    *reinterpret_cast<uint2*>(static_cast<E*>(y) + i) = o;
+  }
+}
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
   const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);

@@ -725,9 +725,9 @@ int tr_plan_tiling(const tr_plan* plan, int64_t tokens, tr_tiling* out) {
   return TR_OK;
 }
 
-int tr_forward_tiled(const tr_plan* plan, const void* packed, const void* x, int64_t tokens,
-                     void* y, void* workspace, size_t workspace_bytes, const tr_tiling* tiling,
-                     void* stream) {
+static int forward_impl(const tr_plan* plan, const void* packed, const void* x, int64_t tokens,
+                        void* y, void* workspace, size_t workspace_bytes,
+                        const tr_tiling* tiling, const Epi& epi, void* stream) {
   int kind;
   MmaGeom g;
   DecodeGeom dg;
@@ -743,8 +743,8 @@ int tr_forward_tiled(const tr_plan* plan, const void* packed, const void* x, int
     set_error("packed, x and y must be 16-byte aligned");
     return TR_ERR_ALIGN;
   }
-  if (kind == KIND_GENERIC) return launch_generic(*plan, packed, x, tokens, y, stream);
-  if (kind == KIND_DECODE) return launch_decode(*plan, dg, packed, x, tokens, y, stream);
+  if (kind == KIND_GENERIC) return launch_generic(*plan, packed, x, tokens, y, stream, epi);
+  if (kind == KIND_DECODE) return launch_decode(*plan, dg, packed, x, tokens, y, stream, epi);
   if (kind == KIND_TC05) {
     if (!workspace || workspace_bytes < tg.ws_bytes) {
       set_error("workspace of %zu bytes needed, %zu given", tg.ws_bytes,
@@ -755,7 +755,7 @@ int tr_forward_tiled(const tr_plan* plan, const void* packed, const void* x, int
       set_error("workspace must be 16-byte aligned");
       return TR_ERR_ALIGN;
     }
-    return launch_tc05(*plan, tg, packed, x, tokens, y, workspace, stream);
+    return launch_tc05(*plan, tg, packed, x, tokens, y, workspace, stream, epi);
   }
   if (g.ws_bytes > 0) {
     if (!workspace || workspace_bytes < g.ws_bytes) {
@@ -768,7 +768,57 @@ int tr_forward_tiled(const tr_plan* plan, const void* packed, const void* x, int
       return TR_ERR_ALIGN;
     }
   }
-  return launch_mma(*plan, g, packed, x, tokens, y, workspace, stream);
+  return launch_mma(*plan, g, packed, x, tokens, y, workspace, stream, epi);
+}
+
+int tr_forward_tiled(const tr_plan* plan, const void* packed, const void* x, int64_t tokens,
+                     void* y, void* workspace, size_t workspace_bytes, const tr_tiling* tiling,
+                     void* stream) {
+  return forward_impl(plan, packed, x, tokens, y, workspace, workspace_bytes, tiling,
+                      Epi{TR_EPI_NONE, 0, 0, nullptr}, stream);
+}
+
+int tr_forward_epilogue(const tr_plan* plan, const void* packed, const void* x, int64_t tokens,
+                        void* y, const tr_epilogue* epilogue, void* workspace,
+                        size_t workspace_bytes, const tr_tiling* tiling, void* stream) {
+  if (!plan) {
+    set_error("null plan");
+    return TR_ERR_INVALID;
+  }
+  Epi epi{TR_EPI_NONE, 0, 0, nullptr};
+  if (epilogue) {
+    const tr_epilogue& e = *epilogue;
+    if (e.kind != TR_EPI_NONE && e.kind != TR_EPI_ADD && e.kind != TR_EPI_SILU_MUL) {
+      set_error("unknown epilogue kind %d", (int)e.kind);
+      return TR_ERR_INVALID;
+    }
+    if (e.out_dtype != TR_F32 && e.out_dtype != plan->dtype) {
+      set_error("epilogue output dtype %d: fp32 or the plan's dtype %d", (int)e.out_dtype,
+                (int)plan->dtype);
+      return TR_ERR_INVALID;
+    }
+    epi.kind = e.kind;
+    epi.out_f32 = e.out_dtype == TR_F32;
+    if (e.kind != TR_EPI_NONE) {
+      if (e.aux_dtype != TR_F32 && e.aux_dtype != plan->dtype) {
+        set_error("epilogue operand dtype %d: fp32 or the plan's dtype %d", (int)e.aux_dtype,
+                  (int)plan->dtype);
+        return TR_ERR_INVALID;
+      }
+      if (tokens > 0 && !e.aux) {
+        set_error("null epilogue operand");
+        return TR_ERR_INVALID;
+      }
+      if ((uintptr_t)e.aux & 15) {
+        set_error("the epilogue operand must be 16-byte aligned");
+        return TR_ERR_ALIGN;
+      }
+      epi.aux_f32 = e.aux_dtype == TR_F32;
+      epi.aux = e.aux;
+    }
+  }
+  return forward_impl(plan, packed, x, tokens, y, workspace, workspace_bytes, tiling, epi,
+                      stream);
 }
 
 int tr_forward(const tr_plan* plan, const void* packed, const void* x, int64_t tokens, void* y,

@@ -143,6 +143,17 @@ struct TcGeom {
   size_t ws_bytes;
 };
 
+// What a kernel writes for output element y[i] = v (v: the fp32 sum of the ring pieces):
+//   kind 0: v;  kind 1: aux[i] + v (residual add);  kind 2: silu(aux[i]) * v (gated MLP);
+// stored as fp32 when out_f32, else in the plan's element type.  aux is [T, d_out] row-major,
+// fp32 when aux_f32, else the plan's element type.
+struct Epi {
+  int kind;
+  int out_f32;
+  int aux_f32;
+  const void* aux;
+};
+
 // Implemented in plan.cpp
 void set_error(const char* fmt, ...);
 int resolve_mma_geom(const Plan& p, int64_t T, const tr_tiling* force, MmaGeom* g);
@@ -151,19 +162,19 @@ void mma_smem_layout(const Plan& p, MmaGeom* g);
 // Implemented in ring_mma.cu / ring_generic.cu / pack.cu
 int launch_pack(const Plan& p, const void* const cores[3], void* packed, void* stream);
 int launch_generic(const Plan& p, const void* packed, const void* x, int64_t T, void* y,
-                   void* stream);
+                   void* stream, const Epi& epi);
 int launch_mma(const Plan& p, const MmaGeom& g, const void* packed, const void* x, int64_t T,
-               void* y, void* ws, void* stream);
+               void* y, void* ws, void* stream, const Epi& epi);
 int query_max_active_clusters(const Plan& p, const MmaGeom& g, int* n);
 int forward_noalloc(const Plan& p, const void* packed, const void* x, int64_t T, void* y,
                     void* stream);
 int resolve_decode_geom(const Plan& p, int64_t T, const tr_tiling* force, DecodeGeom* g);
 int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* force, TcGeom* g);
 int launch_tc05(const Plan& p, const TcGeom& g, const void* packed, const void* x, int64_t T,
-                void* y, void* ws, void* stream);
+                void* y, void* ws, void* stream, const Epi& epi);
 int decode_variant(const Plan& p);
 int decode_max_threads(int variant);
 int launch_decode(const Plan& p, const DecodeGeom& g, const void* packed, const void* x,
-                  int64_t T, void* y, void* stream);
+                  int64_t T, void* y, void* stream, const Epi& epi);
 
 }  // namespace trr

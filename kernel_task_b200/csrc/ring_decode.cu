@@ -45,6 +45,7 @@ struct DecodeParams {
   int warp_bytes;  // per-warp shared area: T1 tile, later the warp's partial Y
   int off_warps;   // offset of the per-warp areas (after the staged G2 chunk)
   int off_recv;    // receive slots of the cluster reduction (CL x slice, fp32)
+  Epi epi;         // what is written for each y element
 };
 
 template <class S, typename E, int RP, int KS1M, int NT1M, int O2CM, int MAXT>
@@ -264,7 +265,6 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
   }
   cluster.sync();  // all partials have landed in their owners' receive slots
   // ---- own slice: add the CL partials in rank order and write y
-  E* y = static_cast<E*>(p.y);
   const int ebeg = crank * SL, eend = min(nout, ebeg + SL);
   for (int e = ebeg + tid; e < eend; e += nthr) {
     float sum = 0.f;
@@ -272,7 +272,8 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
     const int o3 = e % sh.O3, q = e / sh.O3;
     const int o = q % o2n, r = q / o2n;
     const int t = r / sh.O1, o1 = r - t * sh.O1;
-    y[(size_t)t * sh.d_out + o1 * sh.sy1 + (o2a + o) * sh.sy2 + o3 * sh.sy3] = from_f32<E>(sum);
+    epi_store<E>(p.epi, p.y,
+                 (size_t)t * sh.d_out + o1 * sh.sy1 + (o2a + o) * sh.sy2 + o3 * sh.sy3, sum);
   }
 }
 
@@ -319,10 +320,11 @@ int decode_max_threads(int variant) { return variant == 0 ? 512 : (variant == 1 
 
 template <class S>
 static void fill_common(DecodeParams<S>& dp, const Plan& p, const DecodeGeom& g,
-                        const void* packed, const void* x, int64_t T, void* y) {
+                        const void* packed, const void* x, int64_t T, void* y, const Epi& epi) {
   const char* base = static_cast<const char*>(packed);
   dp.x = x;
   dp.y = y;
+  dp.epi = epi;
   dp.g1f = reinterpret_cast<const uint2*>(base + p.m.off_g1);
   dp.g2f = reinterpret_cast<const uint2*>(base + p.m.off_g2);
   dp.g3f = reinterpret_cast<const uint2*>(base + p.m.off_g3);
@@ -364,19 +366,21 @@ static bool shape_matches(const Plan& p) {
 
 template <class S, typename E>
 static cudaError_t launch_decode_fixed(const Plan& p, const DecodeGeom& g, const void* packed,
-                                       const void* x, int64_t T, void* y, cudaStream_t st) {
+                                       const void* x, int64_t T, void* y, const Epi& epi,
+                                       cudaStream_t st) {
   DecodeParams<S> dp;
-  fill_common(dp, p, g, packed, x, T, y);
+  fill_common(dp, p, g, packed, x, T, y, epi);
   constexpr int MAXT = (S::KS1 == 1 && S::NT1 <= 16) ? 512 : (S::KS1 == 1 ? 384 : 256);
   return launch_decode_variant<S, E, S::RPc, S::KS1, S::NT1, 4, MAXT>(dp, g, p.device, st);
 }
 
 template <typename E, int RP>
 static cudaError_t launch_decode_dyn(const Plan& p, const DecodeGeom& g, const void* packed,
-                                     const void* x, int64_t T, void* y, cudaStream_t st) {
+                                     const void* x, int64_t T, void* y, const Epi& epi,
+                                     cudaStream_t st) {
   DecodeParams<DynShape> dp;
   dp.sh = dyn_shape(p);
-  fill_common(dp, p, g, packed, x, T, y);
+  fill_common(dp, p, g, packed, x, T, y, epi);
   switch (decode_variant(p)) {
     case 0: return launch_decode_variant<DynShape, E, RP, 1, 16, 4, 512>(dp, g, p.device, st);
     case 1: return launch_decode_variant<DynShape, E, RP, 1, 32, 4, 384>(dp, g, p.device, st);
@@ -386,23 +390,24 @@ static cudaError_t launch_decode_dyn(const Plan& p, const DecodeGeom& g, const v
 
 template <typename E>
 static cudaError_t launch_decode_e(const Plan& p, const DecodeGeom& g, const void* packed,
-                                   const void* x, int64_t T, void* y, cudaStream_t st) {
+                                   const void* x, int64_t T, void* y, const Epi& epi,
+                                   cudaStream_t st) {
 #define TRR_TRY_FIXED(a, b, c, d, e, f, r, X, Y)                                         \
   if (shape_matches<FixedShape<a, b, c, d, e, f, r, X, Y>>(p))                           \
     return launch_decode_fixed<FixedShape<a, b, c, d, e, f, r, X, Y>, E>(p, g, packed, x, T, \
-                                                                         y, st);
+                                                                         y, epi, st);
   TRR_FIXED_SHAPES(TRR_TRY_FIXED)
 #undef TRR_TRY_FIXED
-  return p.m.RP == 8 ? launch_decode_dyn<E, 8>(p, g, packed, x, T, y, st)
-                     : launch_decode_dyn<E, 16>(p, g, packed, x, T, y, st);
+  return p.m.RP == 8 ? launch_decode_dyn<E, 8>(p, g, packed, x, T, y, epi, st)
+                     : launch_decode_dyn<E, 16>(p, g, packed, x, T, y, epi, st);
 }
 
 int launch_decode(const Plan& p, const DecodeGeom& g, const void* packed, const void* x,
-                  int64_t T, void* y, void* stream) {
+                  int64_t T, void* y, void* stream, const Epi& epi) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const cudaError_t e = p.dtype == TR_F16
-                            ? launch_decode_e<__half>(p, g, packed, x, T, y, st)
-                            : launch_decode_e<__nv_bfloat16>(p, g, packed, x, T, y, st);
+                            ? launch_decode_e<__half>(p, g, packed, x, T, y, epi, st)
+                            : launch_decode_e<__nv_bfloat16>(p, g, packed, x, T, y, epi, st);
   if (e != cudaSuccess) {
     cudaGetLastError();
     set_error("decode kernel launch (chunks=%d CL=%d warps=%d smem=%zu): %s", g.NOC, g.CL, g.NW,

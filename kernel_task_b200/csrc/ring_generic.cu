@@ -28,6 +28,7 @@ struct GenericParams {
   int d_in, d_out;
   long long sx1, sx2, sx3, sy1, sy2, sy3;
   int SC;  // ring indices s per chunk held in shared memory
+  Epi epi;  // what is written for each y element
 };
 
 template <typename E>
@@ -87,15 +88,15 @@ __global__ void __launch_bounds__(256) ring_generic_kernel(GenericParams p) {
     }
   }
   __syncthreads();
-  E* yr = static_cast<E*>(p.y) + (size_t)t * p.d_out + o1 * p.sy1;
+  const size_t yr = (size_t)t * p.d_out + (size_t)o1 * p.sy1;
   for (int e = threadIdx.x; e < nY; e += blockDim.x) {
     const int o3 = e % p.O3, o2 = e / p.O3;
-    yr[o2 * p.sy2 + o3 * p.sy3] = from_f32<E>(Y[e]);
+    epi_store<E>(p.epi, p.y, yr + (size_t)o2 * p.sy2 + (size_t)o3 * p.sy3, Y[e]);
   }
 }
 
 int launch_generic(const Plan& p, const void* packed, const void* x, int64_t T, void* y,
-                   void* stream) {
+                   void* stream, const Epi& epi) {
   const Canon& c = p.c;
   if (p.mma_ok) {
     set_error("fp16/bf16 plans pack the mma layout; the generic kernel needs an fp32 plan or "
@@ -119,6 +120,7 @@ int launch_generic(const Plan& p, const void* packed, const void* x, int64_t T, 
   GenericParams gp;
   gp.x = x;
   gp.y = y;
+  gp.epi = epi;
   gp.g1 = base + p.g.off_g1;
   gp.g2 = base + p.g.off_g2;
   gp.g3 = base + p.g.off_g3;

@@ -57,6 +57,7 @@ struct MmaParams {
   int g2_smem, pf_smem, x_async, g2_bytes;
   int vec4;                 // d_out % 4 == 0: reductions move float4
   int flag_off;
+  Epi epi;                  // what is written for each y element
 };
 
 __device__ __forceinline__ int sel3(int k, int a, int b, int c) {
@@ -312,7 +313,7 @@ __global__ void __launch_bounds__(MAXT, 1) ring_mma_kernel(const MmaParams p) {
 
   // ---- reduce this CTA's slice of the tile over the cluster (loads from every peer issued
   // together, added in rank order), then write y (NC == 1) or this cluster's workspace slot
-  E* y = static_cast<E*>(p.y) + (size_t)t0 * p.d_out;
+  const size_t ybase = (size_t)t0 * p.d_out;
   const size_t sstride = (size_t)p.TT * p.d_out;
   float* slot = p.NC > 1 ? p.slots + ((size_t)tile * p.NC + cl_id) * sstride : nullptr;
   const int vw = p.vec4 ? 4 : 1;
@@ -335,10 +336,8 @@ __global__ void __launch_bounds__(MAXT, 1) ring_mma_kernel(const MmaParams p) {
         s.x += v[r].x; s.y += v[r].y; s.z += v[r].z; s.w += v[r].w;
       }
       if (p.NC == 1) {
-        uint2 o;
-        o.x = pack2<E>(s.x, s.y);
-        o.y = pack2<E>(s.z, s.w);
-        reinterpret_cast<uint2*>(y)[i] = o;
+        const float f[4] = {s.x, s.y, s.z, s.w};
+        epi_store_vec<E, 4>(p.epi, p.y, ybase + 4 * (size_t)i, f);
       } else {
         reinterpret_cast<float4*>(slot)[i] = s;
       }
@@ -352,7 +351,7 @@ __global__ void __launch_bounds__(MAXT, 1) ring_mma_kernel(const MmaParams p) {
 #pragma unroll
       for (int r = 0; r < 16; ++r) s += v[r];
       if (p.NC == 1) {
-        y[i] = from_f32<E>(s);
+        epi_store<E>(p.epi, p.y, ybase + i, s);
       } else {
         slot[i] = s;
       }
@@ -386,10 +385,8 @@ __global__ void __launch_bounds__(MAXT, 1) ring_mma_kernel(const MmaParams p) {
               s.x += v[u].x; s.y += v[u].y; s.z += v[u].z; s.w += v[u].w;
             }
           }
-          uint2 o;
-          o.x = pack2<E>(s.x, s.y);
-          o.y = pack2<E>(s.z, s.w);
-          reinterpret_cast<uint2*>(y)[i] = o;
+          const float f[4] = {s.x, s.y, s.z, s.w};
+          epi_store_vec<E, 4>(p.epi, p.y, ybase + 4 * (size_t)i, f);
         }
       } else {
         for (int i = vbeg + tid; i < vend; i += nthr) {
@@ -402,7 +399,7 @@ __global__ void __launch_bounds__(MAXT, 1) ring_mma_kernel(const MmaParams p) {
 #pragma unroll
             for (int u = 0; u < 8; ++u) s += v[u];
           }
-          y[i] = from_f32<E>(s);
+          epi_store<E>(p.epi, p.y, ybase + i, s);
         }
       }
       if (tid == 0) atomicExch(p.cnt + tile * p.CL + crank, 0);
@@ -467,7 +464,7 @@ static cudaError_t launch_e(const Plan& p, const MmaParams& mp, const MmaGeom& g
 int mma_max_threads(int MTW) { return MTW <= 1 ? 1024 : (MTW <= 2 ? 512 : 384); }
 
 int launch_mma(const Plan& p, const MmaGeom& g, const void* packed, const void* x, int64_t T,
-               void* y, void* ws, void* stream) {
+               void* y, void* ws, void* stream, const Epi& epi) {
   const Canon& c = p.c;
   const MmaLayout& m = p.m;
   if (T > 0x7fffffffLL / std::max(c.d_in, c.d_out)) {
@@ -483,6 +480,7 @@ int launch_mma(const Plan& p, const MmaGeom& g, const void* packed, const void* 
   MmaParams mp;
   mp.x = x;
   mp.y = y;
+  mp.epi = epi;
   mp.g1f = reinterpret_cast<const uint2*>(base + m.off_g1);
   mp.g2f = reinterpret_cast<const uint2*>(base + m.off_g2);
   mp.g3f = reinterpret_cast<const uint2*>(base + m.off_g3);
@@ -608,7 +606,7 @@ int forward_noalloc(const Plan& p, const void* packed, const void* x, int64_t T,
       return TR_ERR_CUDA;
     }
   }
-  return launch_mma(p, g, packed, x, T, y, scratch, stream);
+  return launch_mma(p, g, packed, x, T, y, scratch, stream, Epi{0, 0, 0, nullptr});
 }
 
 }  // namespace trr

@@ -96,6 +96,7 @@ struct TcParams {
   int off_a2, off_b2, off_a3, off_a1, off_g1, off_b3, off_bar;
   int NA2, NA3, NB1, b1_all, NB3, b3_all, a2_bytes, a3_bytes, a1_bytes;
   int ystr, recv_off, vec_out, slot_elems;
+  Epi epi;  // what is written for each y element
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -773,7 +774,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
     }
     cluster.sync();  // every push landed; nobody touches a peer's shared memory after this
   }
-  E* y = static_cast<E*>(p.y) + (size_t)t0 * sh.d_out;
+  const size_t ybase = (size_t)t0 * sh.d_out;
   float* slot = p.NC > 1
       ? p.slots + (((size_t)tile * p.NG + grp) * p.NC + cl_id) * (size_t)p.slot_elems
       : nullptr;
@@ -783,16 +784,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
     const int o3v = e % nper, q = e / nper;
     const int o = q % o2n, r = q / o2n;
     const int t = r / sh.O1, o1 = r - t * sh.O1;
-    E* dst = y + (size_t)t * sh.d_out + o1 * sh.sy1 + (o2a + o) * sh.sy2 + o3v * W * sh.sy3;
+    const size_t i = ybase + (size_t)t * sh.d_out + (size_t)o1 * sh.sy1 +
+                     (size_t)(o2a + o) * sh.sy2 + (size_t)o3v * W * sh.sy3;
     if (p.vec_out) {
-      uint4 out;
-      out.x = pack2<E>(f[0], f[1]);
-      out.y = pack2<E>(f[2], f[3]);
-      out.z = pack2<E>(f[4], f[5]);
-      out.w = pack2<E>(f[6], f[7]);
-      *reinterpret_cast<uint4*>(dst) = out;
+      epi_store_vec<E, 8>(p.epi, p.y, i, f);
     } else {
-      *dst = from_f32<E>(f[0]);
+      epi_store<E>(p.epi, p.y, i, f[0]);
     }
   };
   for (int e = ebeg + tid; e < eend; e += kTcThreads) {
@@ -888,11 +885,12 @@ DynShape dyn_shape(const Plan& p);  // ring_decode.cu
 
 template <class S>
 static void fill_tc(TcParams<S>& tp, const Plan& p, const TcGeom& g, const void* packed,
-                    const void* x, int64_t T, void* y, void* ws) {
+                    const void* x, int64_t T, void* y, void* ws, const Epi& epi) {
   const char* base = static_cast<const char*>(packed);
   const TcLayout& t = p.t;
   tp.x = x;
   tp.y = y;
+  tp.epi = epi;
   tp.b1 = reinterpret_cast<const unsigned char*>(base + t.off_b1);
   tp.b2 = reinterpret_cast<const unsigned char*>(base + t.off_b2);
   tp.b3 = reinterpret_cast<const unsigned char*>(base + t.off_b3);
@@ -945,9 +943,9 @@ static void fill_tc(TcParams<S>& tp, const Plan& p, const TcGeom& g, const void*
 template <class S, typename E>
 static cudaError_t launch_tc_fixed(const Plan& p, const TcGeom& g, const void* packed,
                                    const void* x, int64_t T, void* y, void* ws, int grid,
-                                   cudaStream_t st) {
+                                   const Epi& epi, cudaStream_t st) {
   TcParams<S> tp;
-  fill_tc(tp, p, g, packed, x, T, y, ws);
+  fill_tc(tp, p, g, packed, x, T, y, ws, epi);
   return launch_tc_variant<S, E, S::RPc>(tp, g, p.device, grid, st);
 }
 
@@ -961,29 +959,31 @@ static bool shape_is(const Plan& p) {
 
 template <typename E>
 static cudaError_t launch_tc_e(const Plan& p, const TcGeom& g, const void* packed, const void* x,
-                               int64_t T, void* y, void* ws, int grid, cudaStream_t st) {
+                               int64_t T, void* y, void* ws, int grid, const Epi& epi,
+                               cudaStream_t st) {
 #define TRR_TRY_TC(a, b, c, d, e, f, r, X, Y)                                                    \
   if constexpr (FixedShape<a, b, c, d, e, f, r, X, Y>::RPc <= 16) {                             \
     if (shape_is<FixedShape<a, b, c, d, e, f, r, X, Y>>(p))                                     \
       return launch_tc_fixed<FixedShape<a, b, c, d, e, f, r, X, Y>, E>(p, g, packed, x, T, y,   \
-                                                                       ws, grid, st);          \
+                                                                       ws, grid, epi, st);     \
   }
   TRR_FIXED_SHAPES(TRR_TRY_TC)
 #undef TRR_TRY_TC
   TcParams<DynShape> tp;
   tp.sh = dyn_shape(p);
-  fill_tc(tp, p, g, packed, x, T, y, ws);
+  fill_tc(tp, p, g, packed, x, T, y, ws, epi);
   if (p.m.RP == 8) return launch_tc_variant<DynShape, E, 8>(tp, g, p.device, grid, st);
   return launch_tc_variant<DynShape, E, 16>(tp, g, p.device, grid, st);
 }
 
 int launch_tc05(const Plan& p, const TcGeom& g, const void* packed, const void* x, int64_t T,
-                void* y, void* ws, void* stream) {
+                void* y, void* ws, void* stream, const Epi& epi) {
   const int grid = g.ntiles * p.t.NG * g.CL * g.NC;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const cudaError_t e = p.dtype == TR_F16
-                            ? launch_tc_e<__half>(p, g, packed, x, T, y, ws, grid, st)
-                            : launch_tc_e<__nv_bfloat16>(p, g, packed, x, T, y, ws, grid, st);
+  const cudaError_t e =
+      p.dtype == TR_F16
+          ? launch_tc_e<__half>(p, g, packed, x, T, y, ws, grid, epi, st)
+          : launch_tc_e<__nv_bfloat16>(p, g, packed, x, T, y, ws, grid, epi, st);
   if (e != cudaSuccess) {
     cudaGetLastError();
     set_error("tcgen05 kernel launch (grid=%d CL=%d NC=%d smem=%zu): %s", grid, g.CL, g.NC,

@@ -85,7 +85,9 @@ class RingOp {
     if (st != TR_OK) raise_status(st, "tr_pack_cores");
   }
 
-  at::Tensor forward_impl(const at::Tensor& xin, const tr_tiling* tiling) {
+  at::Tensor forward_impl(const at::Tensor& xin, const tr_tiling* tiling,
+                          int kind = TR_EPI_NONE, const at::Tensor* auxin = nullptr,
+                          bool out_f32 = false) {
     if (xin.dim() != 2 || xin.size(1) != d_in_)
       throw py::value_error("Expected x with shape [tokens, " + std::to_string(d_in_) + "]");
     if (!xin.is_cuda() || xin.get_device() != device_)
@@ -94,9 +96,21 @@ class RingOp {
     if (!packed_.defined()) throw std::runtime_error("cores are not packed");
     const at::Tensor x = xin.is_contiguous() ? xin : xin.contiguous();
     const int64_t T = x.size(0);
+    at::Tensor aux;
+    if (kind != TR_EPI_NONE) {
+      if (!auxin) throw py::value_error("the epilogue needs a second operand");
+      if (auxin->dim() != 2 || auxin->size(0) != T || auxin->size(1) != d_out_)
+        throw py::value_error("Expected the epilogue operand with shape [" + std::to_string(T) +
+                              ", " + std::to_string(d_out_) + "]");
+      if (!auxin->is_cuda() || auxin->get_device() != device_)
+        throw py::value_error("the epilogue operand must be a CUDA tensor on the plan's device");
+      if (auxin->scalar_type() != dtype_ && auxin->scalar_type() != at::kFloat)
+        throw py::value_error("the epilogue operand must be float32 or the cores' dtype");
+      aux = auxin->is_contiguous() ? *auxin : auxin->contiguous();
+    }
     c10::cuda::OptionalCUDAGuard guard;
     if (c10::cuda::current_device() != device_) guard.set_index((c10::DeviceIndex)device_);
-    at::Tensor y = at::empty({T, d_out_}, x.options());
+    at::Tensor y = at::empty({T, d_out_}, x.options().dtype(out_f32 ? at::kFloat : dtype_));
     if (T == 0) return y;
     size_t need = 0;
     int st = tr_workspace_bytes_tiled(plan_.get(), T, tiling, &need);
@@ -106,13 +120,49 @@ class RingOp {
       ws_bytes_ = need;
     }
     cudaStream_t stream = at::cuda::getCurrentCUDAStream((c10::DeviceIndex)device_).stream();
-    st = tr_forward_tiled(plan_.get(), packed_.data_ptr(), x.data_ptr(), T, y.data_ptr(),
-                          ws_bytes_ ? ws_.data_ptr() : nullptr, ws_bytes_, tiling, stream);
-    if (st != TR_OK) raise_status(st, "tr_forward");
+    if (kind == TR_EPI_NONE && !out_f32) {
+      st = tr_forward_tiled(plan_.get(), packed_.data_ptr(), x.data_ptr(), T, y.data_ptr(),
+                            ws_bytes_ ? ws_.data_ptr() : nullptr, ws_bytes_, tiling, stream);
+      if (st != TR_OK) raise_status(st, "tr_forward");
+      return y;
+    }
+    tr_epilogue e;
+    e.kind = kind;
+    e.out_dtype = out_f32 ? TR_F32 : dtype_code(dtype_);
+    e.aux = aux.defined() ? aux.data_ptr() : nullptr;
+    e.aux_dtype = aux.defined() ? dtype_code(aux.scalar_type()) : TR_F32;
+    st = tr_forward_epilogue(plan_.get(), packed_.data_ptr(), x.data_ptr(), T, y.data_ptr(), &e,
+                             ws_bytes_ ? ws_.data_ptr() : nullptr, ws_bytes_, tiling, stream);
+    if (st != TR_OK) raise_status(st, "tr_forward_epilogue");
     return y;
   }
 
   at::Tensor call(const at::Tensor& x) { return forward_impl(x, nullptr); }
+
+  // y in fp32, no rounding to the cores' dtype (the reference's accumulate / forward_fp32)
+  at::Tensor accumulate(const at::Tensor& x) {
+    return forward_impl(x, nullptr, TR_EPI_NONE, nullptr, true);
+  }
+  // h + TR(x) in the cores' dtype (residual add fused into the forward kernel)
+  at::Tensor forward_add(const at::Tensor& x, const at::Tensor& h) {
+    return forward_impl(x, nullptr, TR_EPI_ADD, &h, false);
+  }
+  // silu(g) * TR(x) in the cores' dtype (gated MLP fused into the up projection)
+  at::Tensor forward_silu_mul(const at::Tensor& x, const at::Tensor& g) {
+    return forward_impl(x, nullptr, TR_EPI_SILU_MUL, &g, false);
+  }
+  // any epilogue with an explicit geometry (kernel 0 = planner's choice)
+  at::Tensor call_epilogue(const at::Tensor& x, int64_t kind, c10::optional<at::Tensor> aux,
+                           bool out_fp32, int64_t kernel, int64_t tokens_per_tile,
+                           int64_t cluster, int64_t clusters) {
+    tr_tiling t;
+    t.kernel = (int32_t)kernel;
+    t.tokens_per_tile = (int32_t)tokens_per_tile;
+    t.cluster = (int32_t)cluster;
+    t.clusters = (int32_t)clusters;
+    const at::Tensor* a = aux.has_value() ? &aux.value() : nullptr;
+    return forward_impl(x, kernel ? &t : nullptr, (int)kind, a, out_fp32);
+  }
 
   at::Tensor call_tiled(const at::Tensor& x, int64_t kernel, int64_t tokens_per_tile,
                         int64_t cluster, int64_t clusters) {
@@ -174,6 +224,42 @@ class RingOp {
   size_t ws_bytes_ = 0;
 };
 
+void check_consume_f32(const at::Tensor& t, const at::Tensor& like, const char* what) {
+  if (!t.is_cuda() || t.scalar_type() != at::kFloat || !t.is_contiguous() ||
+      t.sizes() != like.sizes() || t.get_device() != like.get_device())
+    throw py::value_error(std::string(what) + ": FP32 contiguous CUDA tensors of one shape");
+}
+
+// silu(g) * u in `dtype` (bf16 like the reference by default); g and u are cleared
+at::Tensor consume_silu_mul(at::Tensor g, at::Tensor u, at::ScalarType dtype) {
+  check_consume_f32(g, g, "consume_silu_mul");
+  check_consume_f32(u, g, "consume_silu_mul");
+  const int code = dtype_code(dtype);
+  if (code != TR_F16 && code != TR_BF16)
+    throw py::value_error("consume_silu_mul: output dtype float16 or bfloat16");
+  c10::cuda::CUDAGuard guard(g.device());
+  at::Tensor out = at::empty(g.sizes(), g.options().dtype(dtype));
+  const int st = tr_consume_silu_mul(g.data_ptr<float>(), u.data_ptr<float>(), out.data_ptr(),
+                                     code, g.numel(), at::cuda::getCurrentCUDAStream().stream());
+  if (st != TR_OK) raise_status(st, "tr_consume_silu_mul");
+  return out;
+}
+
+// h + y in h's dtype; y (fp32) is cleared
+at::Tensor consume_add(at::Tensor h, at::Tensor y) {
+  check_consume_f32(y, h, "consume_add");
+  const int code = dtype_code(h.scalar_type());
+  if (code != TR_F16 && code != TR_BF16)
+    throw py::value_error("consume_add: h must be float16 or bfloat16");
+  if (!h.is_contiguous()) throw py::value_error("consume_add: h must be contiguous");
+  c10::cuda::CUDAGuard guard(h.device());
+  at::Tensor out = at::empty_like(h);
+  const int st = tr_consume_add(h.data_ptr(), y.data_ptr<float>(), out.data_ptr(), code,
+                                h.numel(), at::cuda::getCurrentCUDAStream().stream());
+  if (st != TR_OK) raise_status(st, "tr_consume_add");
+  return out;
+}
+
 void empty_launch() {
   const int st = tr_empty_launch(at::cuda::getCurrentCUDAStream().stream());
   if (st != TR_OK) raise_status(st, "tr_empty_launch");
@@ -189,6 +275,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            py::arg("device"))
       .def("pack", &RingOp::pack)
       .def("__call__", &RingOp::call)
+      .def("accumulate", &RingOp::accumulate)
+      .def("forward_add", &RingOp::forward_add, py::arg("x"), py::arg("h"))
+      .def("forward_silu_mul", &RingOp::forward_silu_mul, py::arg("x"), py::arg("g"))
+      .def("call_epilogue", &RingOp::call_epilogue, py::arg("x"), py::arg("kind"),
+           py::arg("aux") = py::none(), py::arg("out_fp32") = false, py::arg("kernel") = 0,
+           py::arg("tokens_per_tile") = 0, py::arg("cluster") = 0, py::arg("clusters") = 0)
       .def("call_tiled", &RingOp::call_tiled, py::arg("x"), py::arg("kernel") = 0,
            py::arg("tokens_per_tile") = 0, py::arg("cluster") = 0, py::arg("clusters") = 0)
       .def("tiling", &RingOp::tiling)
@@ -198,4 +290,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_property_readonly("packed", &RingOp::packed)
       .def_property_readonly("workspace", &RingOp::workspace);
   m.def("empty_launch", &empty_launch, "launch an empty kernel on the current stream");
+  m.def("consume_silu_mul", &consume_silu_mul, py::arg("g"), py::arg("u"),
+        py::arg("dtype") = at::kBFloat16, "silu(g) * u (fp32 inputs, cleared) -> dtype");
+  m.def("consume_add", &consume_add, py::arg("h"), py::arg("y"),
+        "h + y (y fp32, cleared) -> h's dtype");
 }

@@ -14,6 +14,16 @@ Differences from the reference, by design:
   * state is one packed-core buffer and, for tilings that reduce across clusters, one
     workspace that every call leaves ready for the next (stream-ordered; one prepared object
     must not be called concurrently from two streams, as in the reference, tr_kernel.py:185).
+
+Model-chain calls on the prepared object (the reference's PreparedTRKernel.accumulate,
+tr_kernel.py:230-243, and its consumers, csrc/v3g/bind.cu:93-156):
+  * ``op.accumulate(x)``         y in fp32 (a new tensor; the reference returns a view of its
+                                 workspace that the consumer must clear);
+  * ``op.forward_add(x, h)``     h + op(x), the residual add done in the forward kernel's store;
+  * ``op.forward_silu_mul(x, g)`` silu(g) * op(x), the gated MLP done in the up projection's
+                                 store (g = gate.accumulate(x), fp32, or the cores' dtype);
+  * ``consume_silu_mul(g, u)`` / ``consume_add(h, y)``: the reference's separate consumers of
+    fp32 outputs (they clear the fp32 inputs, as the reference's do).
 """
 from __future__ import annotations
 
@@ -60,3 +70,15 @@ def prepare_optimized(cores: Sequence[torch.Tensor], spec: TRSpec):
 def tr_forward_optimized(x: torch.Tensor, cores: Sequence[torch.Tensor], spec: TRSpec):
     """One-shot form (submission.py:10-23): prepares, runs once, discards the preparation."""
     return prepare_optimized(cores, spec)(x)
+
+
+def consume_silu_mul(g: torch.Tensor, u: torch.Tensor, dtype: torch.dtype = torch.bfloat16):
+    """silu(g) * u -> ``dtype``; g and u are fp32 [T, N] (N % 4 == 0) and are zero-filled
+    afterwards, as the reference's consumer does (csrc/v3g/bind.cu:123-133)."""
+    return binding().consume_silu_mul(g, u, dtype)
+
+
+def consume_add(h: torch.Tensor, y: torch.Tensor):
+    """h + y -> h's dtype; y is fp32 of h's shape and is zero-filled afterwards
+    (csrc/v3g/bind.cu:135-148)."""
+    return binding().consume_add(h, y)

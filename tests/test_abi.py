@@ -203,3 +203,36 @@ def test_noalloc_entry_point_arguments_need_no_device():
         p = abi.Plan(sp.input_modes, sp.output_modes, sp.rank, abi.TR_F16)
         for T in (1, 2, 3, 5, 8, 16, 32, 64, 128, 1000):
             assert p.workspace_bytes(T) <= (8 << 20)
+
+
+def test_epilogue_and_consumer_arguments_need_no_device():
+    """tr_forward_epilogue and tr_consume_*: argument errors are reported before any CUDA
+    call (the fused forms are checked against the unfused ones on the GPU)."""
+    s = kspec.SPEC_C4["down"]
+    p = abi.Plan(s.input_modes, s.output_modes, s.rank, abi.TR_BF16)
+    E = abi.TrEpilogue
+    fwd = lambda epi, T=1, y=16: p.forward_epilogue(16, 16, T, y, epi)
+    assert fwd(None, T=0) == abi.TR_OK
+    assert fwd(E(abi.TR_EPI_ADD, abi.TR_BF16, 16, abi.TR_F32), T=0) == abi.TR_OK
+    assert fwd(E(7, abi.TR_BF16, 16, abi.TR_BF16)) == abi.TR_ERR_INVALID        # unknown kind
+    assert fwd(E(abi.TR_EPI_NONE, abi.TR_F16, 0, 0)) == abi.TR_ERR_INVALID      # other dtype
+    assert fwd(E(abi.TR_EPI_ADD, abi.TR_F32, 16, abi.TR_F16)) == abi.TR_ERR_INVALID
+    assert fwd(E(abi.TR_EPI_SILU_MUL, abi.TR_BF16, 0, abi.TR_F32)) == abi.TR_ERR_INVALID
+    assert fwd(E(abi.TR_EPI_ADD, abi.TR_BF16, 24, abi.TR_F32)) == abi.TR_ERR_ALIGN
+    assert fwd(E(abi.TR_EPI_ADD, abi.TR_F32, 16, abi.TR_F32), y=0) == abi.TR_ERR_INVALID
+    assert fwd(E(abi.TR_EPI_ADD, abi.TR_F32, 16, abi.TR_F32), T=-1) == abi.TR_ERR_INVALID
+    assert lib_call("tr_forward_epilogue", None, 16, 16, 1, 16, None, None, 0, None,
+                    None) == abi.TR_ERR_INVALID                                  # null plan
+    L = abi.lib()
+    assert L.tr_consume_silu_mul(16, 16, 16, abi.TR_BF16, 0, None) == abi.TR_OK
+    assert L.tr_consume_silu_mul(16, 16, 16, abi.TR_F32, 4, None) == abi.TR_ERR_INVALID
+    assert L.tr_consume_silu_mul(16, 16, 16, abi.TR_BF16, 6, None) == abi.TR_ERR_INVALID
+    assert L.tr_consume_silu_mul(None, 16, 16, abi.TR_F16, 4, None) == abi.TR_ERR_INVALID
+    assert L.tr_consume_silu_mul(16, 20, 16, abi.TR_F16, 4, None) == abi.TR_ERR_ALIGN
+    assert L.tr_consume_add(16, 16, 16, abi.TR_BF16, -4, None) == abi.TR_ERR_INVALID
+    assert L.tr_consume_add(16, 16, 8, abi.TR_BF16, 4, None) == abi.TR_ERR_ALIGN
+    assert L.tr_consume_add(16, 16, 16, 3, 4, None) == abi.TR_ERR_INVALID
+
+
+def lib_call(name, *args):
+    return getattr(abi.lib(), name)(*args)

@@ -14,6 +14,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
 #include <type_traits>
 
 #include "device_util.cuh"
@@ -252,6 +253,67 @@ int launch_pack(const Plan& p, const void* const cores[3], void* packed, void* s
   }
   set_error("unknown dtype");
   return TR_ERR_INVALID;
+}
+
+// ------------------------------------------------------------------------------------------
+// Co-resident cluster counts.  Every kernel of this library holds one CTA per SM (shared memory
+// or registers), so the count depends only on the cluster size; it is measured once per device
+// with an empty kernel that asks for the opt-in shared memory.
+__global__ void cluster_probe_kernel() {}
+
+void query_max_clusters(int device, int num_sms, int out[17]) {
+  static std::mutex mu;
+  static int cache[64][17];
+  static bool have[64] = {};
+  // a 148-SM B200 (measured): 148, 74, -, 33, -, -, -, 15, -, -, -, 7, -, -, -, 7
+  auto fallback = [&](int c) {
+    if (c <= 2) return num_sms / c;
+    if (c <= 4) return (num_sms * 33 / 148) * 4 / c;
+    if (c <= 8) return (num_sms * 15 / 148) * 8 / c;
+    if (c <= 12) return (num_sms * 7 / 148) * 12 / c;
+    return num_sms * 7 / 148;
+  };
+  std::lock_guard<std::mutex> lock(mu);
+  if (device >= 0 && device < 64 && have[device]) {
+    for (int c = 0; c <= 16; ++c) out[c] = cache[device][c];
+    return;
+  }
+  out[0] = 0;
+  for (int c = 1; c <= 16; ++c) out[c] = std::max(1, fallback(c));
+  int cur = -1, smem = 0;
+  if (device < 0 || device >= 64 || cudaGetDevice(&cur) != cudaSuccess ||
+      cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device) !=
+          cudaSuccess) {
+    cudaGetLastError();
+    return;  // no device here: the B200 figures
+  }
+  if (cur != device) cudaSetDevice(device);
+  bool ok = cudaFuncSetAttribute(cluster_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 smem) == cudaSuccess &&
+            cudaFuncSetAttribute(cluster_probe_kernel,
+                                 cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+  for (int c = 1; ok && c <= 16; ++c) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(c * 8));
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)c;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, cluster_probe_kernel, &cfg) == cudaSuccess && n > 0)
+      out[c] = n;
+    else
+      ok = false;
+  }
+  cudaGetLastError();
+  if (cur != device) cudaSetDevice(cur);
+  for (int c = 0; c <= 16; ++c) cache[device][c] = out[c];
+  have[device] = true;
 }
 
 }  // namespace trr

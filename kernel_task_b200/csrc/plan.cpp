@@ -254,6 +254,21 @@ static int max_i3_span(int npieces, int R, int NJ) {
   return best;
 }
 
+// Split NJ-way piece parallelism into clusters of CL CTAs, NC clusters per column of output
+// tiles (`cols` columns), keeping all cols * NC clusters co-resident (one wave): the largest
+// power-of-two cluster (up to cl_max) whose clusters fit, then as many of them as fit.
+static void one_wave_split(const Plan& p, long long cols, int NJ, int cl_max, int* CL, int* NC) {
+  for (int cl = 16; cl >= 1; cl /= 2) {
+    if (cl > cl_max || cl > NJ || cols > p.max_clusters[cl]) continue;
+    *CL = cl;
+    *NC = (int)std::max<long long>(
+        1, std::min<long long>(NJ / cl, p.max_clusters[cl] / std::max(1LL, cols)));
+    return;
+  }
+  *CL = 1;  // more columns than co-resident CTAs: several waves of single CTAs
+  *NC = 1;
+}
+
 int resolve_mma_geom(const Plan& p, int64_t T, const tr_tiling* f, MmaGeom* g) {
   const Canon& c = p.c;
   const MmaLayout& m = p.m;
@@ -294,8 +309,7 @@ int resolve_mma_geom(const Plan& p, int64_t T, const tr_tiling* f, MmaGeom* g) {
   } else {
     int NJ = g->ntiles >= p.num_sms ? 1 : std::max(1, p.num_sms / std::max(1, g->ntiles));
     NJ = std::min(NJ, m.npieces);
-    CL = std::min(8, NJ);
-    NC = std::max(1, NJ / CL);
+    one_wave_split(p, g->ntiles, NJ, 8, &CL, &NC);
   }
   if (CL < 1 || CL > 16 || NC < 1 || (long long)CL * NC > m.npieces) {
     set_error("cluster=%d clusters=%d invalid for %d pieces", CL, NC, m.npieces);
@@ -354,8 +368,9 @@ int resolve_decode_geom(const Plan& p, int64_t T, const tr_tiling* f, DecodeGeom
     set_error("cluster=%d invalid for %d pieces", CL, m.npieces);
     return TR_ERR_INVALID;
   }
+  // default: as many o2 chunks as clusters of CL CTAs fit on the device at once
   int NOC = (f && f->clusters > 0) ? f->clusters
-                                   : std::max(1, std::min(c.O2, p.num_sms / CL));
+                                   : std::max(1, std::min(c.O2, p.max_clusters[CL]));
   int O2C = ceil_div(c.O2, NOC);
   if (O2C > 4) O2C = 4;
   NOC = ceil_div(c.O2, O2C);
@@ -420,8 +435,7 @@ int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* f, TcGeom* g) {
     const long long cols = std::max<long long>(1, (long long)g->ntiles * t.NG);
     int NJ = cols >= p.num_sms ? 1 : (int)std::max<long long>(1, p.num_sms / cols);
     NJ = std::min(NJ, std::max(1, m.npieces / 5));
-    CL = std::min(16, NJ);
-    NC = std::max(1, NJ / CL);
+    one_wave_split(p, cols, NJ, 16, &CL, &NC);
   }
   if (CL < 1 || CL > 16 || NC < 1 || (long long)CL * NC > m.npieces) {
     set_error("cluster=%d clusters=%d invalid for %d pieces", CL, NC, m.npieces);
@@ -590,6 +604,7 @@ int tr_plan_create(const tr_spec* spec, int32_t dtype, int32_t device, tr_plan**
   }
   p->num_sms = nsm;
   p->smem_optin = (size_t)optin;
+  query_max_clusters(device, nsm, p->max_clusters);
   p->tc_ok = 0;
   if (p->mma_ok) build_tc_layout(p);
   if (p->tc_ok) {

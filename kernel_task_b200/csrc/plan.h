@@ -93,7 +93,15 @@ struct Plan {
   size_t packed_bytes;
   int num_sms;
   size_t smem_optin;
+  // max_clusters[c]: thread-block clusters of c CTAs that are co-resident on this device when
+  // every CTA needs a whole SM (the case of every kernel here).  Cluster placement is limited
+  // per GPC, so this is below num_sms / c: 7 clusters of 16 CTAs on a 148-SM B200.
+  int max_clusters[17];
 };
+
+// Fills out[c] (c = 1..16) for `device` by the CUDA occupancy query (cached per process);
+// without a device, the figures of a 148-SM B200.
+void query_max_clusters(int device, int num_sms, int out[17]);
 
 // Geometry of one mma.sync launch (resolved from tr_tiling + the planner).
 struct MmaGeom {

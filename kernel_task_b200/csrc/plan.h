@@ -77,7 +77,14 @@ struct GenericLayout {
   size_t elems_g1, elems_g2, elems_g3;
 };
 
-enum KernelKind { KIND_AUTO = 0, KIND_GENERIC = 1, KIND_MMA = 2, KIND_TC05 = 3, KIND_DECODE = 4 };
+enum KernelKind {
+  KIND_AUTO = 0,
+  KIND_GENERIC = 1,
+  KIND_MMA = 2,
+  KIND_TC05 = 3,
+  KIND_DECODE = 4,
+  KIND_TCS = 5
+};
 
 struct Plan {
   tr_spec spec;
@@ -148,6 +155,23 @@ struct TcGeom {
   size_t a2_bytes, a3_bytes, a1_bytes;
   size_t off_a2, off_b2, off_a3, off_a1, off_g1, off_b3, off_bar;
   size_t smem;
+  size_t part_elems;   // floats of one CTA's partial sums in the workspace (CL > 1)
+  size_t parts_off;    // workspace offset of the per-CTA partial sums
+  size_t ws_bytes;
+};
+
+// Geometry of one launch of the small-T tcgen05 kernel (ring_tcs.cu): NGS sets of NGC o2 groups
+// (O2G modes each), the pieces of each set split over NC clusters of CL CTAs.
+struct TcsGeom {
+  int O2G, NG, NGC, NGS, CL, NC;
+  int MT1;             // 128-row tiles of S1 (rows (o1, u))
+  int N1C, N2C;        // MMA N of S1 (t, i2) and S2 (t, o1), padded to 16
+  int NB, NQ;          // G1/G3 ring slots; x slices staged
+  int d1_col, d2_col, d3_col, tmem_cols;
+  size_t off_a2, off_b1, off_a1, off_b3, off_b2, off_a3, off_ys, off_recv, off_bar;
+  size_t a2_stride, b1_bytes, a1_stride, b3_stride, b2_bytes, a3_stride;
+  int slot_elems;      // floats of one cluster's workspace slot (NC > 1)
+  size_t smem;
   size_t ws_bytes;
 };
 
@@ -178,6 +202,9 @@ int forward_noalloc(const Plan& p, const void* packed, const void* x, int64_t T,
                     void* stream);
 int resolve_decode_geom(const Plan& p, int64_t T, const tr_tiling* force, DecodeGeom* g);
 int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* force, TcGeom* g);
+int resolve_tcs_geom(const Plan& p, int64_t T, const tr_tiling* force, TcsGeom* g);
+int launch_tcs(const Plan& p, const TcsGeom& g, const void* packed, const void* x, int64_t T,
+               void* y, void* ws, void* stream, const Epi& epi);
 int launch_tc05(const Plan& p, const TcGeom& g, const void* packed, const void* x, int64_t T,
                 void* y, void* ws, void* stream, const Epi& epi);
 int decode_variant(const Plan& p);

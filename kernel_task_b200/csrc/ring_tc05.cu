@@ -48,6 +48,7 @@
 #include "device_util.cuh"
 #include "plan.h"
 #include "shapes.cuh"
+#include "tc_util.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -56,8 +57,6 @@ namespace trr {
 constexpr int kTcThreads = 480;
 constexpr int kBuildThreads = 416;  // converter and feeder warps: first x slices
 constexpr int kBarBuild = 1;  // named barrier of the first x slices (0 is __syncthreads)
-constexpr unsigned kWaitLimit = 1u << 16;   // try_wait rounds before a wait gives up
-constexpr unsigned kSuspendNs = 20000;       // suspend-time hint of one try_wait round
 constexpr unsigned kPollLimit = 1u << 24;    // loader polls without progress before it gives up
 constexpr int kA2Slab = 128 * 128;  // bytes of one 64-wide K slab of A2
 
@@ -95,156 +94,11 @@ struct TcParams {
   int b1_bytes, b2_bytes, b3_bytes;
   int off_a2, off_b2, off_a3, off_a1, off_g1, off_b3, off_bar;
   int NA2, NA3, NB1, b1_all, NB3, b3_all, a2_bytes, a3_bytes, a1_bytes;
-  int ystr, recv_off, vec_out, slot_elems;
+  int ystr, vec_out, slot_elems;
+  float* parts;    // per-CTA partial sums in the workspace (CL > 1)
+  int part_elems;  // floats of one CTA's partial sums
   Epi epi;  // what is written for each y element
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-// UMMA shared-memory matrix descriptors (sm_100 version field = 1).
-__device__ __forceinline__ uint64_t desc_plain(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | (uint64_t)((lbo >> 4) & 0x3FFFu) << 16 |
-         (uint64_t)((sbo >> 4) & 0x3FFFu) << 32 | (uint64_t)1 << 46;
-}
-__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | (uint64_t)1 << 16 | (uint64_t)(1024 >> 4) << 32 |
-         (uint64_t)1 << 46 | (uint64_t)2 << 61;
-}
-
-// kind::f16 instruction descriptor: A and B both of type E (fp16 or bf16), fp32 D, K-major.
-template <typename E>
-__host__ __device__ constexpr uint32_t umma_idesc(int M, int N) {
-  return (1u << 4) | ((std::is_same<E, __nv_bfloat16>::value ? 1u : 0u) << 7) |
-         ((std::is_same<E, __nv_bfloat16>::value ? 1u : 0u) << 10) |
-         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-// tcgen05.mma, issued by one elected lane of a converged warp: every lane executes the call with
-// the same operands, so the descriptor arithmetic stays warp-uniform.
-__device__ __forceinline__ void umma_one(uint32_t dtmem, uint64_t da, uint64_t db, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\telect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(
-          dtmem),
-      "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
-}
-__device__ __forceinline__ void commit_one(uint32_t mbar) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(
-          mbar)
-      : "memory");
-}
-
-
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-}
-__device__ __forceinline__ void fence_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-}
-
-__device__ __forceinline__ bool mbar_test(uint32_t mbar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(done)
-      : "r"(mbar), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-// One try_wait round: the thread may be suspended until the phase completes or about
-// kSuspendNs pass, without spinning on the barrier.
-__device__ __forceinline__ bool mbar_try(uint32_t mbar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(done)
-      : "r"(mbar), "r"(parity), "r"(kSuspendNs)
-      : "memory");
-  return done != 0;
-}
-
-// Bounded wait for the phase with parity `parity` to complete.  Gives up at once when the CTA's
-// abort flag is set, and sets it when the bound runs out.
-__device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, volatile int* abort) {
-  if (mbar_test(mbar, parity)) return true;  // already complete: a test costs a few cycles
-  for (unsigned i = 0; i < kWaitLimit; ++i) {
-    if (mbar_try(mbar, parity)) return true;
-    if (*abort) return false;
-  }
-  *abort = 1;
-  return false;
-}
-
-// A converged warp waits together and agrees on the outcome.
-__device__ __forceinline__ bool warp_wait(uint32_t mbar, uint32_t parity, volatile int* abort) {
-  return __all_sync(0xffffffffu, mbar_wait(mbar, parity, abort));
-}
-
-// Bounded wait that ignores the abort flag: draining the CTA's own work in flight.
-__device__ __forceinline__ void mbar_drain(uint32_t mbar, uint32_t parity) {
-  if (mbar_test(mbar, parity)) return;
-  for (unsigned i = 0; i < kWaitLimit && !mbar_try(mbar, parity); ++i) {
-  }
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t mbar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(mbar) : "memory");
-}
-
-// One thread: TMA bulk copy of `bytes` (multiple of 16) global -> shared, completing on `mbar`.
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
-                                          uint32_t mbar) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(mbar), "r"(bytes)
-               : "memory");
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::
-          "r"(dst),
-      "l"(src), "r"(bytes), "r"(mbar)
-      : "memory");
-}
-
-// Named barrier `id` over `n` threads (a multiple of 32): wait for all of them ...
-__device__ __forceinline__ void named_sync(int id, int n) {
-  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory");
-}
-// ... or arrive without waiting (the producer side of a producer -> consumer hand-off).
-__device__ __forceinline__ void named_arrive(int id, int n) {
-  asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(n) : "memory");
-}
-
-template <int N>
-__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]);
-template <>
-__device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
-                 "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
-template <>
-__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-      "%14,%15}, [%16];\n"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-}
 
 // Eight fp32 (as raw TMEM words) -> one 16-byte chunk of fp16.
 __device__ __forceinline__ uint4 chunk_f16(const uint32_t* w) {
@@ -742,37 +596,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   if (tid == 0 && *abort) atomicExch(p.status, (int)TR_ERR_TIMEOUT);
 
   // ---- reduce over the cluster.  Items: 8 consecutive o3 (vector path) or single elements.
-  // Item e of the tile is owned by cluster rank e / SL.  Every CTA pushes each of its partial
-  // items into the owner's receive buffer (recv[sender rank][item], distributed shared-memory
-  // stores, no waiting); after the next cluster barrier each owner adds its items' CL partials from
-  // its own shared memory in rank order, then writes y (one cluster per tile) or its workspace
-  // slot (NC > 1; the last cluster to finish adds the NC slots in cluster order).
+  // Every CTA writes its partial sums to its own workspace area (through L2: far faster than
+  // distributed shared memory for this all-to-all), then after a cluster barrier (release /
+  // acquire at cluster scope) cluster rank r adds items [r SL, (r + 1) SL) of the CL areas in
+  // rank order and writes y (one cluster per tile) or its workspace slot (NC > 1; the last
+  // cluster to finish adds the NC slots in cluster order).
   const int W = p.vec_out ? 8 : 1;  // floats per item
   const int nper = p.vec_out ? sh.O3 / 8 : sh.O3;
   const int nout = rows * o2n * nper;
   const int SL = (nout + p.CL - 1) / p.CL;
   const int ebeg = crank * SL, eend = min(nout, ebeg + SL);
-  float* recv = ys + p.recv_off;
-  auto item_idx = [&](int e) {  // offset of item e inside ys
+  auto item_idx = [&](int e) {  // offset of item e inside ys (and a CTA's partial area)
     const int o3v = e % nper, q = e / nper;
     return (q / o2n) * ystr + (q % o2n) * sh.O3 + o3v * W;
   };
+  const float* parts0 = p.parts + (size_t)(blockIdx.x - crank) * p.part_elems;  // rank 0's
   if (p.CL > 1) {
-    // the receive buffers overlap the peers' operand space: every CTA of the cluster must be
-    // past its piece loop (and have its partial in shared memory) before anyone pushes
+    float4* dst = reinterpret_cast<float4*>(p.parts + (size_t)blockIdx.x * p.part_elems);
+    const float4* src = reinterpret_cast<const float4*>(ys);
+    for (int i = tid; i < rows * ystr / 4; i += kTcThreads) __stcg(dst + i, src[i]);
     cluster.sync();
-    for (int e = tid; e < nout; e += kTcThreads) {
-      const int owner = e / SL, li = e - owner * SL;
-      float* dst = cluster.map_shared_rank(recv, owner) + ((size_t)crank * SL + li) * W;
-      const float* src = ys + item_idx(e);
-      if (p.vec_out) {
-        reinterpret_cast<float4*>(dst)[0] = reinterpret_cast<const float4*>(src)[0];
-        reinterpret_cast<float4*>(dst)[1] = reinterpret_cast<const float4*>(src)[1];
-      } else {
-        *dst = *src;
-      }
-    }
-    cluster.sync();  // every push landed; nobody touches a peer's shared memory after this
   }
   const size_t ybase = (size_t)t0 * sh.d_out;
   float* slot = p.NC > 1
@@ -795,16 +638,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   for (int e = ebeg + tid; e < eend; e += kTcThreads) {
     float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (p.CL > 1) {
-      const float* src = recv + (size_t)(e - ebeg) * W;
+      const float* src = parts0 + item_idx(e);
       for (int k = 0; k < p.CL; ++k) {
-        const float* rk = src + (size_t)k * SL * W;
+        const float* rk = src + (size_t)k * p.part_elems;
         if (p.vec_out) {
-          const float4 u = reinterpret_cast<const float4*>(rk)[0];
-          const float4 w = reinterpret_cast<const float4*>(rk)[1];
+          const float4 u = __ldcg(reinterpret_cast<const float4*>(rk));
+          const float4 w = __ldcg(reinterpret_cast<const float4*>(rk) + 1);
           f[0] += u.x; f[1] += u.y; f[2] += u.z; f[3] += u.w;
           f[4] += w.x; f[5] += w.y; f[6] += w.z; f[7] += w.w;
         } else {
-          f[0] += rk[0];
+          f[0] += __ldcg(rk);
         }
       }
     } else {
@@ -933,7 +776,8 @@ static void fill_tc(TcParams<S>& tp, const Plan& p, const TcGeom& g, const void*
   tp.a3_bytes = (int)g.a3_bytes;
   tp.a1_bytes = (int)g.a1_bytes;
   tp.ystr = g.ystr;
-  tp.recv_off = 128 * g.ystr;  // floats: the receive buffers follow the partial y
+  tp.parts = reinterpret_cast<float*>(static_cast<char*>(ws) + g.parts_off);
+  tp.part_elems = (int)g.part_elems;
   const Canon& c = p.c;
   tp.vec_out = c.sy3 == 1 && c.O3 % 8 == 0 && c.sy1 % 8 == 0 && c.sy2 % 8 == 0 &&
                c.d_out % 8 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;

@@ -55,6 +55,16 @@ __device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t w) {
   return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
 }
 
+// ---- programmatic dependent launch: the kernels are launched so that they may start while
+// the previous kernel of the stream finishes.  pdl_wait() blocks until that kernel completed
+// and its memory is visible; every global-memory access of a kernel comes after it.
+// pdl_trigger() lets the next kernel of the stream start (its own pdl_wait still waits for
+// this whole grid).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
 // ---- output epilogue (struct Epi, plan.h): the value written for y[i], and the store
 template <typename E, class EP>
 __device__ __forceinline__ float epi_value(const EP& ep, size_t i, float v) {

@@ -61,6 +61,7 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
   const int crank = (int)cluster.block_rank();
   // announce that this CTA runs; the matching wait precedes the first remote store
   asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+  pdl_wait();  // launched while the previous kernel finishes: no global access before this
   const int chunk = blockIdx.x / p.CL;
   const int o2a = chunk * p.O2C;
   const int o2n = min(p.O2C, sh.O2 - o2a);
@@ -231,6 +232,7 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
     __syncthreads();
   }
 
+  pdl_trigger();  // the next kernel may set up while this one reduces
   // ---- warp partial -> its shared area (rows (t,o1), columns (o2 of chunk, o3))
   __syncwarp();
 #pragma unroll
@@ -298,13 +300,15 @@ static cudaError_t launch_decode_variant(const DecodeParams<S>& dp, const Decode
   cfg.blockDim = dim3((unsigned)(g.NW * 32));
   cfg.dynamicSmemBytes = g.smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)g.CL;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kern, dp);
 }
 

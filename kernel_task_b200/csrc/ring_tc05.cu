@@ -221,6 +221,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // TMEM, barriers and pads were set up while the previous kernel finished
   const uint32_t tmem = *tmem_slot;
   const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
 
@@ -527,6 +528,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
     }
   }
 
+  pdl_trigger();  // the next kernel may set up while this one reduces
   // ---- D3 -> partial y of this CTA (rows (t,o1), columns (o of group, o3)), fp32 in smem.
   // D3DONE: every tensor-core operation completed, so the operand space is free.
   __syncthreads();
@@ -714,13 +716,15 @@ static cudaError_t launch_tc_variant(const TcParams<S>& tp, const TcGeom& g, int
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = g.smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)g.CL;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kern, tp);
 }
 

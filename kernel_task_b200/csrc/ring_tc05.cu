@@ -26,9 +26,12 @@
 // soon as its TMEM loads of a piece have landed (D1READ, D2READ: the accumulator buffer may be
 // overwritten by the next S1) and when the piece's operand is written (C1DONE, C2DONE).  The
 // issuers start the next S1 first, so the converters never wait for MMA issue; the tensor-core
-// stages signal their consumers with one tcgen05.commit each (S1DONE, S2DONE, S3DONE).  After the last piece D3 is summed across the cluster's CTAs through
-// distributed shared memory (and across clusters through workspace slots when NC > 1) and
-// written as y.
+// stages signal their consumers with one tcgen05.commit each (S1DONE, S2DONE, S3DONE).  After
+// the last piece D3 is summed across the cluster's CTAs through per-CTA workspace areas in L2
+// (and across clusters through workspace slots when NC > 1) and written as y.  The kernel is
+// launched with programmatic stream serialization: its set-up (TMEM, barriers, pads) overlaps
+// the previous kernel of the stream, and no thread touches global memory before
+// griddepcontrol.wait.
 //
 // Shared-memory operand layouts (K-major):
 //   A2  128-byte swizzle: 64-element K slabs of 128 rows x 128 B, row groups 1024 B apart, the

@@ -92,7 +92,10 @@ void tr_plan_destroy(tr_plan* plan);
 int tr_packed_bytes(const tr_plan* plan, size_t* bytes);
 
 /* Pack the three caller cores (contiguous device tensors of the plan's dtype, shapes
- * [R,o_k,i_k,R]) into `packed`.  Cores are read, never written.  Stream-ordered.             */
+ * [R,o_k,i_k,R]) into `packed`.  Cores are read, never written.  Stream-ordered.
+ * The forward kernels may start their first reads of `packed` while the previous kernel of the
+ * stream is still running (programmatic dependent launch); write a packed buffer only through
+ * this call (it ends with a normally serialized launch), or with a stream-ordered copy.      */
 int tr_pack_cores(const tr_plan* plan, const void* const cores[3], void* packed, void* stream);
 
 /* Workspace bytes tr_forward needs for `tokens` rows (0 when the chosen kernel needs none).

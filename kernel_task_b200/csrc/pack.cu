@@ -238,6 +238,11 @@ static int pack_typed(const Plan& p, const void* const cores[3], void* packed, c
   return TR_OK;
 }
 
+// Launched (normally, without programmatic serialization) after the pack kernels: the forward
+// kernels read packed cores before their griddepcontrol.wait, which is safe because the packed
+// buffer is written only here and this launch cannot start before the pack kernels completed.
+__global__ void pack_fence_kernel() {}
+
 int launch_pack(const Plan& p, const void* const cores[3], void* packed, void* stream) {
   int cur = -1;
   if (cudaGetDevice(&cur) != cudaSuccess || cur != p.device) {
@@ -246,13 +251,21 @@ int launch_pack(const Plan& p, const void* const cores[3], void* packed, void* s
     return TR_ERR_INVALID;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int r = TR_ERR_INVALID;
   switch (p.dtype) {
-    case TR_F32: return pack_typed<float>(p, cores, packed, st);
-    case TR_F16: return pack_typed<__half>(p, cores, packed, st);
-    case TR_BF16: return pack_typed<__nv_bfloat16>(p, cores, packed, st);
+    case TR_F32: r = pack_typed<float>(p, cores, packed, st); break;
+    case TR_F16: r = pack_typed<__half>(p, cores, packed, st); break;
+    case TR_BF16: r = pack_typed<__nv_bfloat16>(p, cores, packed, st); break;
+    default: set_error("unknown dtype"); return TR_ERR_INVALID;
   }
-  set_error("unknown dtype");
-  return TR_ERR_INVALID;
+  if (r != TR_OK) return r;
+  pack_fence_kernel<<<1, 32, 0, st>>>();
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("pack launch: %s", cudaGetErrorString(e));
+    return TR_ERR_CUDA;
+  }
+  return TR_OK;
 }
 
 // ------------------------------------------------------------------------------------------

@@ -29,9 +29,9 @@
 // stages signal their consumers with one tcgen05.commit each (S1DONE, S2DONE, S3DONE).  After
 // the last piece D3 is summed across the cluster's CTAs through per-CTA workspace areas in L2
 // (and across clusters through workspace slots when NC > 1) and written as y.  The kernel is
-// launched with programmatic stream serialization: its set-up (TMEM, barriers, pads) overlaps
-// the previous kernel of the stream, and no thread touches global memory before
-// griddepcontrol.wait.
+// launched with programmatic stream serialization: its set-up (TMEM, barriers, pads) and the
+// first bulk copies of packed cores overlap the previous kernel of the stream; x, y and the
+// workspace are touched only after griddepcontrol.wait.
 //
 // Shared-memory operand layouts (K-major):
 //   A2  128-byte swizzle: 64-element K slabs of 128 rows x 128 B, row groups 1024 B apart, the
@@ -224,7 +224,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  pdl_wait();  // TMEM, barriers and pads were set up while the previous kernel finished
   const uint32_t tmem = *tmem_slot;
   const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
 
@@ -266,9 +265,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
     return true;
   };
 
+  // Programmatic dependent launch: TMEM, barriers and pads were set up while the previous kernel
+  // of the stream finished; every thread waits for it (griddepcontrol.wait) before its first
+  // access to x, y or the workspace.  Only the packed cores are read earlier, by the feeder's
+  // first bulk copies: they are written by nothing but tr_pack_cores, which ends with a normally
+  // serialized launch.
   if (warp == 12) {
     // ===================== issuer A: S2 of each piece (and S1, separate buffers) ==============
     // The whole warp runs the loop (uniform decisions); one elected lane issues.
+    pdl_wait();
     bool ok = true, b2ok = false;
     if (np > 0) {  // the first S1s: as many as there are D1 buffers
       const int first = p.shared_d12 ? 2 : p.ND1;
@@ -304,6 +309,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
     __syncwarp();
   } else if (warp == 13) {
     // ===================== issuer B: S3 of each piece (and S1, shared buffers) ================
+    pdl_wait();
     bool ok = true;
     const uint32_t sbo3 = (uint32_t)(K3 / 8) * 128;
     const uint32_t idesc3 = umma_idesc<__half>(128, p.N3P);
@@ -354,6 +360,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
       }
     }
     __syncwarp();
+    pdl_wait();
     for (int q = 0; q < 2 && q < nq; ++q)
       build_a1(sh, smem + p.off_a1 + q * p.a1_bytes, xt, TTv, i3a + q, bt, kBuildThreads);
     fence_async_smem();

@@ -10,6 +10,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <string>
 
@@ -621,7 +622,23 @@ static int pick_kind(const Plan& p, int64_t T, const tr_tiling* f) {
 
 using namespace trr;
 
-struct tr_plan : public trr::Plan {};
+// The geometry the planner picks for a token count, cached per plan (the reference caches its
+// tiling per T as well, tr_kernel.py:250-253): a forward call resolves it twice (workspace size,
+// launch), and the tcgen05 planner walks buffer-depth options.  Only default tilings that
+// resolved are cached; a small direct-mapped table keyed by T.
+struct GeomCacheEntry {
+  int64_t tokens = -1;
+  int kind = 0;
+  trr::MmaGeom g;
+  trr::DecodeGeom dg;
+  trr::TcGeom tg;
+  trr::TcsGeom sg;
+};
+
+struct tr_plan : public trr::Plan {
+  mutable std::mutex cache_mu;
+  mutable GeomCacheEntry cache[32];
+};
 
 extern "C" {
 
@@ -742,6 +759,9 @@ int tr_plan_flops_per_token(const tr_plan* plan, double* flops) {
   return TR_OK;
 }
 
+static int resolve_geom(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling, int* kind,
+                        MmaGeom* g, DecodeGeom* dg, TcGeom* tg, TcsGeom* sg);
+
 static int geom_for(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling, int* kind,
                     MmaGeom* g, DecodeGeom* dg, TcGeom* tg, TcsGeom* sg) {
   if (!plan) {
@@ -752,6 +772,34 @@ static int geom_for(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling
     set_error("negative token count");
     return TR_ERR_INVALID;
   }
+  if (!tiling && tokens > 0) {
+    std::lock_guard<std::mutex> lock(plan->cache_mu);
+    const GeomCacheEntry& e = plan->cache[(uint64_t)tokens % 32];
+    if (e.tokens == tokens) {
+      *kind = e.kind;
+      *g = e.g;
+      *dg = e.dg;
+      *tg = e.tg;
+      *sg = e.sg;
+      return TR_OK;
+    }
+  }
+  const int st = resolve_geom(plan, tokens, tiling, kind, g, dg, tg, sg);
+  if (st == TR_OK && !tiling && tokens > 0) {
+    std::lock_guard<std::mutex> lock(plan->cache_mu);
+    GeomCacheEntry& e = plan->cache[(uint64_t)tokens % 32];
+    e.tokens = tokens;
+    e.kind = *kind;
+    e.g = *g;
+    e.dg = *dg;
+    e.tg = *tg;
+    e.sg = *sg;
+  }
+  return st;
+}
+
+static int resolve_geom(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling, int* kind,
+                        MmaGeom* g, DecodeGeom* dg, TcGeom* tg, TcsGeom* sg) {
   *kind = pick_kind(*plan, tokens, tiling);
   if (*kind == KIND_MMA) {
     if (tokens == 0) {

@@ -199,11 +199,13 @@ def test_noalloc_entry_point_arguments_need_no_device():
     assert p16.forward_noalloc(0, 16, 1, 16) == abi.TR_ERR_INVALID
     assert p16.forward_noalloc(16, 24, 1, 16) == abi.TR_ERR_ALIGN
     assert p32.forward_noalloc(16, 16, 1, 16) == abi.TR_ERR_UNSUPPORTED
-    # the planner's geometry fits the built-in scratch for every benchmark shape and size
+    # the mma kernel's default geometry (the one the no-alloc entry point runs) fits the
+    # built-in scratch for every benchmark shape and size
+    mma = abi.TrTiling(kernel=abi.KERNEL_MMA)
     for sp in (kspec.SPEC_C1, kspec.SPEC_C2, *kspec.SPEC_C4.values()):
         p = abi.Plan(sp.input_modes, sp.output_modes, sp.rank, abi.TR_F16)
         for T in (1, 2, 3, 5, 8, 16, 32, 64, 128, 1000):
-            assert p.workspace_bytes(T) <= (8 << 20)
+            assert p.workspace_bytes(T, mma) <= (8 << 20)
 
 
 def test_epilogue_and_consumer_arguments_need_no_device():

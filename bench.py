@@ -63,6 +63,13 @@ def parse():
     return ap.parse_args()
 
 
+def reference_flops(spec):
+    """FLOPs per token by the reference's own count, 2(ni nj nk P R^2 + nj nk P Q R^3 +
+    P Q Rr nk R^2) (tools/measure_kernels.py:36-44), reported beside the chosen order's."""
+    (ni, nj, nk), (P, Q, Rr), R = spec.input_modes, spec.output_modes, spec.rank
+    return 2 * (ni * nj * nk * P * R * R + nj * nk * P * Q * R ** 3 + P * Q * Rr * nk * R * R)
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -414,11 +421,19 @@ def run_ours(args, rank, world, local_rank):
         cores = baseline_cores(spec, seed=0, dtype=torch.float16, device=dev)
         x = baseline_x(spec, T, seed=0, dtype=torch.float16, device=dev)
         torch.cuda.synchronize()
+        base_mem = torch.cuda.memory_allocated(dev)
+        torch.cuda.reset_peak_memory_stats(dev)
         t0 = time.perf_counter()
         fn = prepare_optimized(cores, spec)
         torch.cuda.synchronize()
         prep_ms = (time.perf_counter() - t0) * 1e3
-        cases[(R, T)] = {"spec": spec, "cores": cores, "x": x, "fn": fn, "prep_ms": prep_ms}
+        t0 = time.perf_counter()
+        fn(x)
+        torch.cuda.synchronize()
+        first_ms = (time.perf_counter() - t0) * 1e3
+        peak = torch.cuda.max_memory_allocated(dev) - base_mem  # packed cores, workspace, y
+        cases[(R, T)] = {"spec": spec, "cores": cores, "x": x, "fn": fn, "prep_ms": prep_ms,
+                         "first_ms": first_ms, "peak_mem": int(peak)}
 
     if world > 1:
         torch.distributed.barrier()
@@ -453,6 +468,12 @@ def run_ours(args, rank, world, local_rank):
         c["flops"] = c["fn"].flops_per_token() * c["x"].shape[0]
         c["tiling"] = c["fn"].tiling(c["x"].shape[0])
 
+    # the launch floor: an empty kernel of this library, same legs (cold: after the L2 flush)
+    from kernel_task_b200._native import binding
+
+    empty = binding().empty_launch
+    launch_cold = statistics.mean(cold_device_us(lambda _v: empty(), None, flush, steps, warmup))
+    launch_warm = warm_stream_us(lambda _v: empty(), None)
     prefill = (prefill_leg(args, rank, world, dev, tc_peak) if args.prefill_tokens > 0
                else None)
     chain = (decode_chain_leg(dev, args.chain_layers)
@@ -464,6 +485,15 @@ def run_ours(args, rank, world, local_rank):
     e2e = max_over_ranks([statistics.mean(cases[k]["e2e"]) for k in keys], world)
     if rank != 0:
         return
+    # binding floor per case: max(launch floor, compulsory bytes / HBM, FLOPs / tensor peak)
+    floors, warm_floors = [], []
+    for k in keys:
+        c = cases[k]
+        spec_k, T_k = c["spec"], k[1]
+        bytes_k = 2 * (spec_k.factor_parameters + T_k * (spec_k.in_features + spec_k.out_features))
+        work = max(bytes_k / (hbm_peak * 1e9) * 1e6, c["flops"] / (tc_peak * 1e12) * 1e6)
+        floors.append(max(launch_cold, work))
+        warm_floors.append(max(launch_warm, work))
     per_case = {}
     for i, k in enumerate(keys):
         c = cases[k]
@@ -482,6 +512,11 @@ def run_ours(args, rank, world, local_rank):
             "tflops": round(c["flops"] / (mean[i] * 1e-6) / 1e12, 2),
             "tiling": c["tiling"], "packed_bytes": int(c["fn"].packed.numel()),
             "workspace_bytes": int(c["fn"].workspace_bytes(T)),
+            "first_call_ms": round(c["first_ms"], 3), "peak_mem_bytes": c["peak_mem"],
+            "flops_reference_formula": reference_flops(spec) * T,
+            "floor_us": round(floors[i], 3), "frac_of_floor": round(floors[i] / mean[i], 4),
+            "warm_floor_us": round(warm_floors[i], 3),
+            "warm_frac_of_floor": round(warm_floors[i] / c["warm"], 4),
         }
     # roofline of the dominant kernel: the case with the largest device time
     dom = max(range(len(keys)), key=lambda i: mean[i])
@@ -506,6 +541,8 @@ def run_ours(args, rank, world, local_rank):
                 "h2d_bytes_per_step": sum(cases[k]["h2d"] for k in keys),
                 "d2h_bytes_per_step": sum(cases[k]["d2h"] for k in keys)},
         "gpu_launches": launches,
+        "launch_floor_us": {"cold": round(launch_cold, 3), "warm_stream": round(launch_warm, 3),
+                            "kernel": "trr empty kernel (tr_empty_launch)"},
         "roofline": {"bound": "tensor",
                      "kernel": f"{KERNEL_NAMES.get(cases[dk]['tiling']['kernel'], '?')} "
                                f"r{dk[0]} t{dk[1]}",

@@ -379,9 +379,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
       bool ok = true;
       for (int j = 0; j < np; ++j) {
         const int ab = j % p.NA2;
-        if (ok) ok = mbar_wait(bar(BAR_S1DONE + (j & 3)), (j >> 2) & 1, abort);
+        if (ok) ok = mbar_spin(bar(BAR_S1DONE + (j & 3)), (j >> 2) & 1, abort);
         if (ok && j >= p.NA2)  // S2 of the piece that last used this A2 buffer completed
-          ok = mbar_wait(bar(BAR_S2DONE + ((j - p.NA2) & 1)), ((j - p.NA2) >> 1) & 1, abort);
+          ok = mbar_spin(bar(BAR_S2DONE + ((j - p.NA2) & 1)), ((j - p.NA2) >> 1) & 1, abort);
         bool d1_read = false;
         if (ok) {
           unsigned char* a2 = smem + p.off_a2 + ab * p.a2_bytes;
@@ -440,9 +440,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
       bool ok = true;
       for (int j = 0; j < np; ++j) {
         const int db = j & 1, ab = j % p.NA3;
-        if (ok) ok = mbar_wait(bar(BAR_S2DONE + db), (j >> 1) & 1, abort);
+        if (ok) ok = mbar_spin(bar(BAR_S2DONE + db), (j >> 1) & 1, abort);
         if (ok && j >= p.NA3)  // S3 of the piece that last used this A3 buffer completed
-          ok = mbar_wait(bar(BAR_S3DONE + ((j - p.NA3) & 15)), ((j - p.NA3) >> 4) & 1, abort);
+          ok = mbar_spin(bar(BAR_S3DONE + ((j - p.NA3) & 15)), ((j - p.NA3) >> 4) & 1, abort);
         if (ok) {
           const uint32_t d2 = tmem + lane_base + d2_col(j);
           unsigned char* rowp =

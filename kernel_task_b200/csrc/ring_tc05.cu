@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   const S& sh = p.sh;
   constexpr int K3 = 16;         // S3 K (v padded to 16)
   constexpr int NCH = RP / 8;    // 16-byte chunks of one (o1 or o2, i2) run of RP values
-  constexpr int CB = 5;          // 16-column TMEM loads per wait in C1 and C2 (80 columns)
+  constexpr int CB = 5;          // 16-column TMEM loads per wait in C1 (80 columns)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -447,18 +447,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
           const uint32_t d2 = tmem + lane_base + d2_col(j);
           unsigned char* rowp =
               smem + p.off_a3 + ab * p.a3_bytes + (r >> 3) * ((K3 / 8) * 128) + (r & 7) * 16;
-          for (int c0 = 0; c0 < p.N2; c0 += 16 * CB) {
-            uint32_t v[CB][16];
+          // rank 16: the 96 columns of the widest group (O2G = 6) in one wait (-2.7 us on c2
+          // T = 32 against two); rank 8 groups are at most 48 columns
+          constexpr int CB2 = RP == 16 ? 6 : CB;
+          for (int c0 = 0; c0 < p.N2; c0 += 16 * CB2) {
+            uint32_t v[CB2][16];
 #pragma unroll
-            for (int c = 0; c < CB; ++c)
+            for (int c = 0; c < CB2; ++c)
               if (c0 + c * 16 < p.N2) tmem_ld<16>(d2 + c0 + c * 16, v[c]);
             tmem_wait_ld();
-            if (c0 + 16 * CB >= p.N2) {  // last read of D2(j): its buffer may be reused
+            if (c0 + 16 * CB2 >= p.N2) {  // last read of D2(j): its buffer may be reused
               __syncwarp();
               if (lane == 0) mbar_arrive(bar(BAR_D2READ + db));
             }
 #pragma unroll
-            for (int c = 0; c < CB; ++c) {
+            for (int c = 0; c < CB2; ++c) {
 #pragma unroll
               for (int hh = 0; hh < 2; ++hh) {
                 const int col = c0 + c * 16 + 8 * hh;  // D2 column = o * RP + v

@@ -548,7 +548,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   float* ys = reinterpret_cast<float*>(smem);
   const int ystr = p.ystr;
   if (warp < 12) {
-    const bool ok = np > 0 && mbar_wait(bar(BAR_D3DONE), 0, abort);
+    const bool ok = np > 0 && mbar_spin(bar(BAR_D3DONE), 0, abort);
     tc_fence_after();
     const int r = 32 * (warp & 3) + lane;
     const bool vec4 = (sh.O3 & 3) == 0;

@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(kTcsThreads, 1) ring_tcs_kernel(const TcsParam
   int issued = min(p.NB, np);  // pieces whose operands were requested (thread 0's count)
   // every thread waits for the commit of warp 0's latest batch of MMAs
   auto batch_wait = [&]() {
-    mbar_wait(bar(TBAR_MM), mm_phase, abort);
+    mbar_spin(bar(TBAR_MM), mm_phase, abort);
     mm_phase ^= 1u;
     tc_fence_after();
   };

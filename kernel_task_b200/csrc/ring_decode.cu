@@ -259,9 +259,18 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
     const int o3 = e % sh.O3, q = e / sh.O3;
     const int o = q % o2n, r = q / o2n;
     const int idx = r * YSTR + o * sh.O3P + o3;
+    // every warp's value in flight at once, then added in warp order
+    constexpr int kMaxWarps = MAXT / 32;
+    float part[kMaxWarps];
+#pragma unroll
+    for (int w = 0; w < kMaxWarps; ++w)
+      part[w] = w < nwarps
+                    ? reinterpret_cast<const float*>(smem + p.off_warps + w * p.warp_bytes)[idx]
+                    : 0.f;
     float v = 0.f;
-    for (int w = 0; w < nwarps; ++w)
-      v += reinterpret_cast<const float*>(smem + p.off_warps + w * p.warp_bytes)[idx];
+#pragma unroll
+    for (int w = 0; w < kMaxWarps; ++w)
+      if (w < nwarps) v += part[w];
     const int owner = e / SL;
     cluster.map_shared_rank(recv, owner)[crank * SL + (e - owner * SL)] = v;
   }
@@ -269,8 +278,13 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
   // ---- own slice: add the CL partials in rank order and write y
   const int ebeg = crank * SL, eend = min(nout, ebeg + SL);
   for (int e = ebeg + tid; e < eend; e += nthr) {
+    float rk[16];  // the CL partials in flight at once, added in rank order
+#pragma unroll
+    for (int k = 0; k < 16; ++k) rk[k] = k < p.CL ? recv[k * SL + (e - ebeg)] : 0.f;
     float sum = 0.f;
-    for (int k = 0; k < p.CL; ++k) sum += recv[k * SL + (e - ebeg)];
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+      if (k < p.CL) sum += rk[k];
     const int o3 = e % sh.O3, q = e / sh.O3;
     const int o = q % o2n, r = q / o2n;
     const int t = r / sh.O1, o1 = r - t * sh.O1;

@@ -61,7 +61,11 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
   const int crank = (int)cluster.block_rank();
   // announce that this CTA runs; the matching wait precedes the first remote store
   asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
-  pdl_wait();  // launched while the previous kernel finishes: no global access before this
+  // Programmatic dependent launch: the kernel may start while the previous kernel of the stream
+  // finishes.  The packed cores (G2 staging, G1/G3 fragments) are read before griddepcontrol.wait
+  // (they are written by nothing but tr_pack_cores, which ends with a normally serialized launch);
+  // x, y and the epilogue operand only after it.
+  bool waited = false;
   const int chunk = blockIdx.x / p.CL;
   const int o2a = chunk * p.O2C;
   const int o2n = min(p.O2C, sh.O2 - o2a);
@@ -125,6 +129,10 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
         b3[k][n] = (active && n < sh.NT3)
                        ? __ldg(p.g3f + (((size_t)pi * KS3 + k) * sh.NT3 + n) * 32 + lane)
                        : make_uint2(0u, 0u);
+    if (!waited) {  // first piece: the previous kernel's x is complete and visible from here
+      pdl_wait();
+      waited = true;
+    }
     // x A fragments: rows (t, i2) = 16*mt + g (+8), columns i1 = 16*k + 2*t4 (+1, +8, +9)
     uint32_t xa[2][KS1M][4];
 #pragma unroll
@@ -227,6 +235,7 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
     }
     __syncwarp();  // T1 fully read before the next piece overwrites it
   }
+  if (!waited) pdl_wait();
   if (!g2_ready) {  // warps without pieces still take part in the CTA barrier
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     __syncthreads();

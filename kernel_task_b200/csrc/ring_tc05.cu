@@ -653,16 +653,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   for (int e = ebeg + tid; e < eend; e += kTcThreads) {
     float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (p.CL > 1) {
+      // four ranks' partials in flight at once (an L2 round trip each), added in rank order
       const float* src = parts0 + item_idx(e);
-      for (int k = 0; k < p.CL; ++k) {
-        const float* rk = src + (size_t)k * p.part_elems;
+      for (int k0 = 0; k0 < p.CL; k0 += 4) {
         if (p.vec_out) {
-          const float4 u = __ldcg(reinterpret_cast<const float4*>(rk));
-          const float4 w = __ldcg(reinterpret_cast<const float4*>(rk) + 1);
-          f[0] += u.x; f[1] += u.y; f[2] += u.z; f[3] += u.w;
-          f[4] += w.x; f[5] += w.y; f[6] += w.z; f[7] += w.w;
+          float4 u[4], w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float4* rk =
+                reinterpret_cast<const float4*>(src + (size_t)(k0 + i) * p.part_elems);
+            if (k0 + i < p.CL) { u[i] = __ldcg(rk); w[i] = __ldcg(rk + 1); }
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            if (k0 + i < p.CL) {
+              f[0] += u[i].x; f[1] += u[i].y; f[2] += u[i].z; f[3] += u[i].w;
+              f[4] += w[i].x; f[5] += w[i].y; f[6] += w[i].z; f[7] += w[i].w;
+            }
+          }
         } else {
-          f[0] += __ldcg(rk);
+          float v[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (k0 + i < p.CL) v[i] = __ldcg(src + (size_t)(k0 + i) * p.part_elems);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (k0 + i < p.CL) f[0] += v[i];
         }
       }
     } else {

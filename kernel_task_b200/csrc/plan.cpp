@@ -280,6 +280,49 @@ static void one_wave_split(const Plan& p, long long cols, int NJ, int cl_max, in
   *NC = best_nc;
 }
 
+// Split of the tcgen05 kernel's pieces: for each tile column (`cols` of them, `rows` rows
+// (t, o1) each), CL CTAs per cluster and NC clusters, chosen among the splits whose cols * NC
+// clusters are all co-resident (one wave) by an estimate of the device time that depends on
+// the split, in microseconds:
+//   * the longest piece range of a CTA times the cost of one piece's S1 -> C1 -> S2 -> C2 -> S3
+//     chain, which the C1 conversion of N1P columns per row sets (0.9 us at 80 columns, 1.4 at
+//     160 with D1 and D2 in shared TMEM buffers);
+//   * 1 us when a CTA's range crosses an i3 boundary (a second x slice to stage);
+//   * with NC > 1, 2 us for the cross-cluster slot pass plus the slot traffic of a CTA,
+//     NC / CL of a tile's partial sums (1.4 us per 69 KB).
+// At most 5 clusters per column.  Fitted to forced splits of the 1920 -> 2880 ring (R 8 and 16)
+// at T = 4-32; against the earlier rule (most CTAs, at most 4 clusters per column, at least 5
+// pieces per CTA) every split it changes on the benchmark and config-4 shapes measured equal or
+// faster: c1 T = 8 -1.4 us, c2 T = 32 -2 us, config-4 k T = 8 -3.7 us, down T = 8 -9.7 us, gate
+// T = 32 -14 us.
+static void tc_split(const Plan& p, long long cols, int64_t rows, int* CL, int* NC) {
+  const Canon& c = p.c;
+  const MmaLayout& m = p.m;
+  const TcLayout& t = p.t;
+  const double piece_us =
+      t.shared_d12 ? 1.4 : 0.5 + 0.005 * t.N1P;
+  const double part_kb = (double)rows * t.O2G * c.O3 * 4 / 1024.0;
+  double best = 1e30;
+  *CL = 1;
+  *NC = 1;
+  for (int cl = 16; cl >= 1; cl /= 2) {
+    if (cl > m.npieces || cols > p.max_clusters[cl]) continue;
+    const long long nc_max =
+        std::min<long long>(std::min<long long>(p.max_clusters[cl] / cols, m.npieces / cl), 5);
+    for (int nc = 1; nc <= nc_max; ++nc) {
+      const int NJ = cl * nc;
+      double est = piece_us * ceil_div(m.npieces, NJ) +
+                   1.0 * (max_i3_span(m.npieces, c.R, NJ) - 1);
+      if (nc > 1) est += 2.0 + 1.4 * ((double)nc / cl) * part_kb / 67.5;
+      if (est < best - 1e-9) {
+        best = est;
+        *CL = cl;
+        *NC = nc;
+      }
+    }
+  }
+}
+
 int resolve_mma_geom(const Plan& p, int64_t T, const tr_tiling* f, MmaGeom* g) {
   const Canon& c = p.c;
   const MmaLayout& m = p.m;
@@ -441,12 +484,8 @@ int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* f, TcGeom* g) {
     CL = f->cluster;
     NC = f->clusters > 0 ? f->clusters : 1;
   } else {
-    // one wave of CTAs, but at least ~5 pieces per CTA: below that the fixed prologue and
-    // reduction cost more than the extra parallelism saves
     const long long cols = std::max<long long>(1, (long long)g->ntiles * t.NG);
-    int NJ = cols >= p.num_sms ? 1 : (int)std::max<long long>(1, p.num_sms / cols);
-    NJ = std::min(NJ, std::max(1, m.npieces / 5));
-    one_wave_split(p, cols, NJ, 16, &CL, &NC);
+    tc_split(p, cols, std::min<int64_t>(T, TT) * c.O1, &CL, &NC);
   }
   if (CL < 1 || CL > 16 || NC < 1 || (long long)CL * NC > m.npieces) {
     set_error("cluster=%d clusters=%d invalid for %d pieces", CL, NC, m.npieces);

@@ -698,13 +698,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
     }
   }
   if (p.NC > 1) {
-    __threadfence();
+    // the CTA barrier orders every thread's slot stores before thread 0's fence and count (a
+    // release at device scope); thread 0's fence after the count orders the last cluster's slot
+    // reads after it (an acquire), and the barrier passes that on to the other threads
     __syncthreads();
     int* counter = p.cnt + ((size_t)tile * p.NG + grp) * p.CL + crank;
-    if (tid == 0) *flag = (atomicAdd(counter, 1) == p.NC - 1);
+    if (tid == 0) {
+      __threadfence();
+      *flag = (atomicAdd(counter, 1) == p.NC - 1);
+      __threadfence();
+    }
     __syncthreads();
     if (*flag) {  // last cluster for this slice: add the NC slots in cluster order, write y
-      __threadfence();
       for (int e = ebeg + tid; e < eend; e += kTcThreads) {
         float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         for (int c = 0; c < p.NC; ++c) {

@@ -138,6 +138,36 @@ def test_geometry_and_workspace():
         p.workspace_bytes(1, too_many)
 
 
+# clusters of 1/2/4/8/16 CTAs co-resident on a B200 (the planner's table without a device)
+B200_CLUSTERS = {1: 148, 2: 74, 4: 33, 8: 15, 16: 7}
+
+
+@pytest.mark.parametrize("name", ["c1", "c2", "q", "k", "gate", "down"])
+def test_tcgen05_split_stays_in_one_wave(name):
+    """Every default tcgen05 split keeps all its clusters co-resident (at most 5 per column) and
+    gives each CTA at least one piece."""
+    s = {"c1": kspec.SPEC_C1, "c2": kspec.SPEC_C2}.get(name) or kspec.SPEC_C4[name]
+    p = abi.Plan(s.input_modes, s.output_modes, s.rank, abi.TR_BF16)
+    d = json.loads(p.describe())
+    for T in (2, 3, 8, 17, 32, 64, 200, 4096):
+        t = p.tiling(T)
+        if t.kernel != abi.KERNEL_TC05:
+            continue
+        cols = -(-T // t.tokens_per_tile) * d["groups"]
+        assert 1 <= t.clusters <= 5 and t.cluster * t.clusters <= d["pieces"]
+        if cols <= B200_CLUSTERS[1]:
+            assert cols * t.clusters <= B200_CLUSTERS[t.cluster], (T, t.cluster, t.clusters)
+
+
+def test_tcgen05_split_on_benchmark_shapes():
+    """The splits measured fastest among forced splits on B200 (c1 T8: 5 clusters of 8; c2 T32:
+    5 clusters of 4; c1 T32: one cluster of 16)."""
+    want = {(kspec.SPEC_C1, 8): (8, 5), (kspec.SPEC_C2, 32): (4, 5), (kspec.SPEC_C1, 32): (16, 1)}
+    for (s, T), (cl, nc) in want.items():
+        t = abi.Plan(s.input_modes, s.output_modes, s.rank, abi.TR_F16).tiling(T)
+        assert (t.kernel, t.cluster, t.clusters) == (abi.KERNEL_TC05, cl, nc)
+
+
 def test_forward_argument_errors_need_no_device():
     s = kspec.SPEC_C1
     p = abi.Plan(s.input_modes, s.output_modes, s.rank, abi.TR_F16)

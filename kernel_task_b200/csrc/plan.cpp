@@ -402,16 +402,18 @@ int resolve_mma_geom(const Plan& p, int64_t T, const tr_tiling* f, MmaGeom* g) {
   return TR_OK;
 }
 
-// Decode geometry: S2 rows (t, o1) fit one m16 tile.  Clusters of CL CTAs split the pieces;
-// NOC clusters split the output modes o2 into chunks of O2C (<= 4, the kernel's capacity).
+// Decode geometry: S2 rows (t, o1) fit one or two m16 tiles.  Clusters of CL CTAs split the
+// pieces; NOC clusters split the output modes o2 into chunks of O2C (at most the compiled
+// kernel's capacity: 4 with one row tile, 2 or 1 with two).
 int resolve_decode_geom(const Plan& p, int64_t T, const tr_tiling* f, DecodeGeom* g) {
   const Canon& c = p.c;
   const MmaLayout& m = p.m;
   const int variant = decode_variant(p);
-  if (!p.mma_ok || variant < 0 || T < 1 || T * c.O1 > 16) {
-    set_error("decode kernel needs T*O1 <= 16, rank <= 16 and an fp16/bf16 plan");
+  if (!p.mma_ok || variant < 0 || T < 1 || T * c.O1 > 32) {
+    set_error("decode kernel needs T*O1 <= 32, rank <= 16 and an fp16/bf16 plan");
     return TR_ERR_UNSUPPORTED;
   }
+  g->MT2 = ceil_div((int)T * c.O1, 16);
   g->MT1 = ceil_div((int)T * c.I2, 16);
   if (g->MT1 > 2) {
     set_error("decode kernel: %lld tokens x %d S1 rows exceed two m16 tiles", (long long)T, c.I2);
@@ -425,15 +427,16 @@ int resolve_decode_geom(const Plan& p, int64_t T, const tr_tiling* f, DecodeGeom
   // default: as many o2 chunks as clusters of CL CTAs fit on the device at once
   int NOC = (f && f->clusters > 0) ? f->clusters
                                    : std::max(1, std::min(c.O2, p.max_clusters[CL]));
+  const int o2c_max = decode_max_o2c(variant, g->MT2);
   int O2C = ceil_div(c.O2, NOC);
-  if (O2C > 4) O2C = 4;
+  if (O2C > o2c_max) O2C = o2c_max;
   NOC = ceil_div(c.O2, O2C);
-  const int maxw = decode_max_threads(variant) / 32;
+  const int maxw = decode_max_threads(variant, g->MT2) / 32;
   const int ppc = ceil_div(m.npieces, CL);
   g->CL = CL;
   g->NW = std::min(ppc, maxw);
-  const size_t t1 = (size_t)16 * (m.K2P + 8) * 2;
-  const size_t yw = (size_t)16 * 4 * m.O3P * 4;
+  const size_t t1 = (size_t)16 * g->MT2 * (m.K2P + 8) * 2;
+  const size_t yw = (size_t)16 * g->MT2 * o2c_max * m.O3P * 4;
   g->warp_bytes = align_up(std::max(t1, yw), 16);
   for (;;) {
     g->O2C = O2C;
@@ -659,7 +662,9 @@ static int pick_kind(const Plan& p, int64_t T, const tr_tiling* f) {
   if (f && f->kernel != KIND_AUTO) return f->kernel;
   if (p.mma_ok) {
     DecodeGeom d;
-    if (T >= 1 && T * p.c.O1 <= 16 && resolve_decode_geom(p, T, nullptr, &d) == TR_OK)
+    // the decode kernel while S2's rows (t, o1) fit two m16 tiles (and S1's rows two): at T = 2-3
+    // on c1/c2 it takes half the tcgen05 kernel's time (c2 T = 2: 14.5 against 26.8 us cold)
+    if (T >= 1 && T * p.c.O1 <= 32 && resolve_decode_geom(p, T, nullptr, &d) == TR_OK)
       return KIND_DECODE;
     TcGeom tg;
     if (T >= 1 && p.tc_ok && resolve_tc_geom(p, T, nullptr, &tg) == TR_OK) return KIND_TC05;

@@ -137,6 +137,7 @@ struct DecodeGeom {
   int O2C;       // o2 modes per cluster
   int NW;        // warps per CTA (one piece per warp at a time)
   int MT1;       // m16 tiles of S1 rows (t, i2): 1 or 2
+  int MT2;       // m16 tiles of S2/S3 rows (t, o1): 1 or 2
   size_t warp_bytes;  // per-warp shared area (T1 tile, then the warp's partial Y)
   size_t off_warps;   // after the staged G2 chunk
   size_t off_recv;    // cluster-reduction receive slots, after the warp areas
@@ -208,7 +209,8 @@ int launch_tcs(const Plan& p, const TcsGeom& g, const void* packed, const void* 
 int launch_tc05(const Plan& p, const TcGeom& g, const void* packed, const void* x, int64_t T,
                 void* y, void* ws, void* stream, const Epi& epi);
 int decode_variant(const Plan& p);
-int decode_max_threads(int variant);
+int decode_max_threads(int variant, int mt2);
+int decode_max_o2c(int variant, int mt2);
 int launch_decode(const Plan& p, const DecodeGeom& g, const void* packed, const void* x,
                   int64_t T, void* y, void* stream, const Epi& epi);
 

@@ -1,6 +1,6 @@
 // Decode kernel: the fused tensor-ring operator for token counts whose S2 rows (t, o1) fit one
-// m16 tile (T * O1 <= 16; T = 1 for every benchmark shape).  One launch, no workspace, no
-// global atomics, deterministic summation order.
+// or two m16 tiles (T * O1 <= 32: T = 1 for every benchmark shape, T = 2-3 for small decode
+// batches).  One launch, no workspace, no global atomics, deterministic summation order.
 //
 // Work split (canonical form, plan.h):
 //   * a warp owns one ring piece (i3, s) at a time and runs the whole chain for it:
@@ -40,6 +40,7 @@ struct DecodeParams {
   const uint2* g3f;
   int T;
   int MT1;         // m16 tiles of S1 rows (t, i2)
+  int MT2;         // m16 tiles of S2/S3 rows (t, o1): 1 or 2
   int CL;          // CTAs per cluster (pieces split over them)
   int O2C;         // o2 modes per cluster
   int warp_bytes;  // per-warp shared area: T1 tile, later the warp's partial Y
@@ -48,7 +49,7 @@ struct DecodeParams {
   Epi epi;         // what is written for each y element
 };
 
-template <class S, typename E, int RP, int KS1M, int NT1M, int O2CM, int MAXT>
+template <class S, typename E, int RP, int KS1M, int NT1M, int O2CM, int MAXT, int MT2M>
 __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams<S> p) {
   const S& sh = p.sh;
   constexpr int NV = RP / 8;
@@ -73,7 +74,7 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
   const int pb = (int)((long long)(crank + 1) * sh.npieces / p.CL);
   const int T1STR = sh.K2P + 8;
   const int YSTR = O2CM * sh.O3P;          // partial Y row: this chunk's (o2, o3)
-  const int rows = p.T * sh.O1;            // valid S2 rows (t, o1), <= 16
+  const int rows = p.T * sh.O1;            // valid S2 rows (t, o1), <= 16 * MT2M
   const int s1rows = p.T * sh.I2;          // valid S1 rows (t, i2)
 
   // ---- stage this chunk's G2 fragments: per k-step, O2C*NV contiguous n-tiles
@@ -97,13 +98,15 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
     for (int i = lane; i < p.warp_bytes / 16; i += 32) z[i] = make_uint4(0u, 0u, 0u, 0u);
   }
 
-  float yacc[O2CM][4][4];
+  float yacc[MT2M][O2CM][4][4];
 #pragma unroll
-  for (int a = 0; a < O2CM; ++a)
+  for (int m = 0; m < MT2M; ++m)
 #pragma unroll
-    for (int b = 0; b < 4; ++b)
+    for (int a = 0; a < O2CM; ++a)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) yacc[a][b][c] = 0.f;
+      for (int b = 0; b < 4; ++b)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) yacc[m][a][b][c] = 0.f;
 
   const E* x = static_cast<const E*>(p.x);
   bool g2_ready = false;
@@ -185,50 +188,54 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
       __syncthreads();
       g2_ready = true;
     }
-    // ---- S2 for every o2 of the chunk, A fragments shared across them
-    float d2[O2CM][NV][4];
+    // ---- S2 and S3 per m16 tile of rows (t, o1); S2's A fragments shared across the o2
 #pragma unroll
-    for (int a = 0; a < O2CM; ++a)
+    for (int mt = 0; mt < MT2M; ++mt) {
+      if (mt * 16 >= rows) break;
+      float d2[O2CM][NV][4];
 #pragma unroll
-      for (int b = 0; b < NV; ++b)
+      for (int a = 0; a < O2CM; ++a)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) d2[a][b][c] = 0.f;
-    const uint2* g2s = reinterpret_cast<const uint2*>(smem) + lane;
-    for (int ks = 0; ks < sh.KS2; ++ks) {
-      uint32_t a[4];
-      ldsm_x4(a, t1 + (size_t)(lane & 15) * T1STR + ks * 16 + (lane >> 4) * 8);
+        for (int b = 0; b < NV; ++b)
 #pragma unroll
-      for (int o = 0; o < O2CM; ++o) {
-        if (o < o2n) {
+          for (int c = 0; c < 4; ++c) d2[a][b][c] = 0.f;
+      const uint2* g2s = reinterpret_cast<const uint2*>(smem) + lane;
+      for (int ks = 0; ks < sh.KS2; ++ks) {
+        uint32_t a[4];
+        ldsm_x4(a, t1 + (size_t)(mt * 16 + (lane & 15)) * T1STR + ks * 16 + (lane >> 4) * 8);
 #pragma unroll
-          for (int nv = 0; nv < NV; ++nv) {
-            const uint2 b = g2s[((size_t)ks * o2n * NV + o * NV + nv) * 32];
-            mma_16816(d2[o][nv], a, b.x, b.y, __half());
+        for (int o = 0; o < O2CM; ++o) {
+          if (o < o2n) {
+#pragma unroll
+            for (int nv = 0; nv < NV; ++nv) {
+              const uint2 b = g2s[((size_t)ks * o2n * NV + o * NV + nv) * 32];
+              mma_16816(d2[o][nv], a, b.x, b.y, __half());
+            }
           }
         }
       }
-    }
-    // ---- S3
+      // ---- S3
 #pragma unroll
-    for (int o = 0; o < O2CM; ++o) {
-      if (o < o2n) {
-        if constexpr (RP == 8) {
-          const uint32_t a0 = pack2<__half>(d2[o][0][0], d2[o][0][1]);
-          const uint32_t a1 = pack2<__half>(d2[o][0][2], d2[o][0][3]);
-#pragma unroll
-          for (int n = 0; n < 4; ++n)
-            if (n < sh.NT3) mma_1688(yacc[o][n], a0, a1, b3[0][n].x);
-        } else {
-#pragma unroll
-          for (int k = 0; k < KS3; ++k) {
-            uint32_t a[4];
-            a[0] = pack2<__half>(d2[o][2 * k][0], d2[o][2 * k][1]);
-            a[1] = pack2<__half>(d2[o][2 * k][2], d2[o][2 * k][3]);
-            a[2] = pack2<__half>(d2[o][2 * k + 1][0], d2[o][2 * k + 1][1]);
-            a[3] = pack2<__half>(d2[o][2 * k + 1][2], d2[o][2 * k + 1][3]);
+      for (int o = 0; o < O2CM; ++o) {
+        if (o < o2n) {
+          if constexpr (RP == 8) {
+            const uint32_t a0 = pack2<__half>(d2[o][0][0], d2[o][0][1]);
+            const uint32_t a1 = pack2<__half>(d2[o][0][2], d2[o][0][3]);
 #pragma unroll
             for (int n = 0; n < 4; ++n)
-              if (n < sh.NT3) mma_16816(yacc[o][n], a, b3[k][n].x, b3[k][n].y, __half());
+              if (n < sh.NT3) mma_1688(yacc[mt][o][n], a0, a1, b3[0][n].x);
+          } else {
+#pragma unroll
+            for (int k = 0; k < KS3; ++k) {
+              uint32_t a[4];
+              a[0] = pack2<__half>(d2[o][2 * k][0], d2[o][2 * k][1]);
+              a[1] = pack2<__half>(d2[o][2 * k][2], d2[o][2 * k][3]);
+              a[2] = pack2<__half>(d2[o][2 * k + 1][0], d2[o][2 * k + 1][1]);
+              a[3] = pack2<__half>(d2[o][2 * k + 1][2], d2[o][2 * k + 1][3]);
+#pragma unroll
+              for (int n = 0; n < 4; ++n)
+                if (n < sh.NT3) mma_16816(yacc[mt][o][n], a, b3[k][n].x, b3[k][n].y, __half());
+            }
           }
         }
       }
@@ -245,17 +252,19 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
   // ---- warp partial -> its shared area (rows (t,o1), columns (o2 of chunk, o3))
   __syncwarp();
 #pragma unroll
-  for (int o = 0; o < O2CM; ++o)
+  for (int mt = 0; mt < MT2M; ++mt)
 #pragma unroll
-    for (int n = 0; n < 4; ++n)
+    for (int o = 0; o < O2CM; ++o)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int r = g + 8 * h;
-        const int col = o * sh.O3P + n * 8 + 2 * t4;
-        if (r < rows && n < sh.NT3)
-          *reinterpret_cast<float2*>(yw + (size_t)r * YSTR + col) =
-              make_float2(yacc[o][n][2 * h], yacc[o][n][2 * h + 1]);
-      }
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = mt * 16 + g + 8 * h;
+          const int col = o * sh.O3P + n * 8 + 2 * t4;
+          if (r < rows && n < sh.NT3)
+            *reinterpret_cast<float2*>(yw + (size_t)r * YSTR + col) =
+                make_float2(yacc[mt][o][n][2 * h], yacc[mt][o][n][2 * h + 1]);
+        }
   __syncthreads();
   // ---- push: sum the warps (fixed order) for each output of the chunk and store the CTA's
   // partial into the owning CTA's receive slot (distributed shared memory).  Output e of the
@@ -303,10 +312,10 @@ __global__ void __launch_bounds__(MAXT, 1) ring_decode_kernel(const DecodeParams
 }
 
 // ------------------------------------------------------------------------------------------
-template <class S, typename E, int RP, int KS1M, int NT1M, int O2CM, int MAXT>
+template <class S, typename E, int RP, int KS1M, int NT1M, int O2CM, int MAXT, int MT2M>
 static cudaError_t launch_decode_variant(const DecodeParams<S>& dp, const DecodeGeom& g,
                                          int device, cudaStream_t st) {
-  auto kern = ring_decode_kernel<S, E, RP, KS1M, NT1M, O2CM, MAXT>;
+  auto kern = ring_decode_kernel<S, E, RP, KS1M, NT1M, O2CM, MAXT, MT2M>;
   static bool configured[64] = {};
   if (device >= 0 && device < 64 && !configured[device]) {
     int optin = 0;
@@ -317,7 +326,7 @@ static cudaError_t launch_decode_variant(const DecodeParams<S>& dp, const Decode
     if (e != cudaSuccess) return e;
     configured[device] = true;
   }
-  if (g.NW * 32 > MAXT) return cudaErrorInvalidConfiguration;
+  if (g.NW * 32 > MAXT || g.O2C > O2CM || g.MT2 > MT2M) return cudaErrorInvalidConfiguration;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(g.NOC * g.CL));
   cfg.blockDim = dim3((unsigned)(g.NW * 32));
@@ -335,7 +344,10 @@ static cudaError_t launch_decode_variant(const DecodeParams<S>& dp, const Decode
   return cudaLaunchKernelEx(&cfg, kern, dp);
 }
 
-// Variant = (S1 k-steps, S1 n-tiles) capacity: (1,16) 512 threads, (1,32) 384, (2,32) 256.
+// Variant = (S1 k-steps, S1 n-tiles) capacity: (1,16), (1,32), (2,32).  Threads per CTA and
+// o2 modes per cluster the compiled kernels hold, by variant and S2 row tiles (MT2): one row
+// tile 512 / 384 / 256 threads with 4 o2; two row tiles (twice the accumulators) 384 / 256 / 256
+// threads with 2 / 2 / 1 o2.
 int decode_variant(const Plan& p) {
   if (p.m.KS1 > 2 || p.m.NT1 > 32 || p.m.RP > 16) return -1;
   if (p.m.KS1 == 1 && p.m.NT1 <= 16) return 0;
@@ -343,7 +355,12 @@ int decode_variant(const Plan& p) {
   return 2;
 }
 
-int decode_max_threads(int variant) { return variant == 0 ? 512 : (variant == 1 ? 384 : 256); }
+int decode_max_threads(int variant, int mt2) {
+  if (mt2 > 1) return variant == 0 ? 384 : 256;
+  return variant == 0 ? 512 : (variant == 1 ? 384 : 256);
+}
+
+int decode_max_o2c(int variant, int mt2) { return mt2 > 1 ? (variant == 2 ? 1 : 2) : 4; }
 
 template <class S>
 static void fill_common(DecodeParams<S>& dp, const Plan& p, const DecodeGeom& g,
@@ -357,6 +374,7 @@ static void fill_common(DecodeParams<S>& dp, const Plan& p, const DecodeGeom& g,
   dp.g3f = reinterpret_cast<const uint2*>(base + p.m.off_g3);
   dp.T = (int)T;
   dp.MT1 = g.MT1;
+  dp.MT2 = g.MT2;
   dp.CL = g.CL;
   dp.O2C = g.O2C;
   dp.warp_bytes = (int)g.warp_bytes;
@@ -397,8 +415,12 @@ static cudaError_t launch_decode_fixed(const Plan& p, const DecodeGeom& g, const
                                        cudaStream_t st) {
   DecodeParams<S> dp;
   fill_common(dp, p, g, packed, x, T, y, epi);
-  constexpr int MAXT = (S::KS1 == 1 && S::NT1 <= 16) ? 512 : (S::KS1 == 1 ? 384 : 256);
-  return launch_decode_variant<S, E, S::RPc, S::KS1, S::NT1, 4, MAXT>(dp, g, p.device, st);
+  constexpr int V = (S::KS1 == 1 && S::NT1 <= 16) ? 0 : (S::KS1 == 1 ? 1 : 2);
+  if (g.MT2 > 1)
+    return launch_decode_variant<S, E, S::RPc, S::KS1, S::NT1, V == 2 ? 1 : 2,
+                                 V == 0 ? 384 : 256, 2>(dp, g, p.device, st);
+  return launch_decode_variant<S, E, S::RPc, S::KS1, S::NT1, 4,
+                               V == 0 ? 512 : (V == 1 ? 384 : 256), 1>(dp, g, p.device, st);
 }
 
 template <typename E, int RP>
@@ -408,10 +430,17 @@ static cudaError_t launch_decode_dyn(const Plan& p, const DecodeGeom& g, const v
   DecodeParams<DynShape> dp;
   dp.sh = dyn_shape(p);
   fill_common(dp, p, g, packed, x, T, y, epi);
+  if (g.MT2 > 1) {
+    switch (decode_variant(p)) {
+      case 0: return launch_decode_variant<DynShape, E, RP, 1, 16, 2, 384, 2>(dp, g, p.device, st);
+      case 1: return launch_decode_variant<DynShape, E, RP, 1, 32, 2, 256, 2>(dp, g, p.device, st);
+      default: return launch_decode_variant<DynShape, E, RP, 2, 32, 1, 256, 2>(dp, g, p.device, st);
+    }
+  }
   switch (decode_variant(p)) {
-    case 0: return launch_decode_variant<DynShape, E, RP, 1, 16, 4, 512>(dp, g, p.device, st);
-    case 1: return launch_decode_variant<DynShape, E, RP, 1, 32, 4, 384>(dp, g, p.device, st);
-    default: return launch_decode_variant<DynShape, E, RP, 2, 32, 4, 256>(dp, g, p.device, st);
+    case 0: return launch_decode_variant<DynShape, E, RP, 1, 16, 4, 512, 1>(dp, g, p.device, st);
+    case 1: return launch_decode_variant<DynShape, E, RP, 1, 32, 4, 384, 1>(dp, g, p.device, st);
+    default: return launch_decode_variant<DynShape, E, RP, 2, 32, 4, 256, 1>(dp, g, p.device, st);
   }
 }
 

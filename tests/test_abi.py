@@ -118,9 +118,11 @@ def test_geometry_and_workspace():
     assert t.kernel == abi.KERNEL_DECODE and t.tokens_per_tile == 1
     assert p.workspace_bytes(1) == 0          # the decode kernel reduces inside its clusters
     assert p.workspace_bytes(0) == 0
-    for T in (2, 8, 32, 33, 1000):
+    for T in (2, 3):                             # two m16 tiles of rows (t, o1)
+        assert p.tiling(T).kernel == abi.KERNEL_DECODE and p.workspace_bytes(T) == 0
+    for T in (4, 8, 32, 33, 1000):
         t = p.tiling(T)
-        assert t.kernel == abi.KERNEL_TC05       # tensor-core kernel once T * o1 > 16
+        assert t.kernel == abi.KERNEL_TC05       # tensor-core kernel once T * o1 > 32
         ws = p.workspace_bytes(T)
         assert ws >= 256                         # status word (+ counters)
         # per-CTA partial sums (cluster > 1) and slots across clusters (clusters > 1)

@@ -7,6 +7,8 @@ counts, independent prepared weights, the five required CUDA workloads) and its 
 """
 from __future__ import annotations
 
+import json
+
 import numpy as np
 import pytest
 import torch
@@ -147,6 +149,53 @@ def test_decode_chain_layers(name, T):
     ref = oracle.tr_forward_reference(x.float().cpu().numpy(),
                                       [c.float().cpu().numpy() for c in cores])
     check_close(fn(x), ref, torch.bfloat16)
+
+
+# the decode kernel with two m16 tiles of S2 rows (16 < T*O1 <= 32): small decode batches on the
+# benchmark shapes (fp16) and the config-4 q/gate layers (bf16), and odd shapes of several ring
+# orders (run-time shapes)
+DECODE2 = {
+    "c1": (kspec.SPEC_C1, torch.float16), "c2": (kspec.SPEC_C2, torch.float16),
+    "q": (kspec.SPEC_C4["q"], torch.bfloat16), "gate": (kspec.SPEC_C4["gate"], torch.bfloat16),
+    "odd": (kspec.TRSpec((2, 3, 4), (5, 6, 7), 3), torch.float16),
+    "odd_cba": (kspec.TRSpec((6, 5, 12), (7, 6, 9), 11), torch.float16),
+    "odd_bac": (kspec.TRSpec((5, 7, 6), (9, 3, 10), 13), torch.bfloat16),
+}
+
+
+@pytest.mark.parametrize("name,T", [("c1", 2), ("c1", 3), ("c2", 2), ("c2", 3), ("q", 2),
+                                    ("gate", 2), ("odd", 3), ("odd", 4), ("odd_cba", 2),
+                                    ("odd_cba", 3), ("odd_bac", 6)])
+@pytest.mark.parametrize("geom", [(0, 0), (16, 3), (4, 12), (5, 2)])
+def test_decode_two_row_tiles(name, T, geom):
+    s, dtype = DECODE2[name]
+    cores = kspec.baseline_cores(s, seed=7, dtype=dtype, device=DEV)
+    fn = prepare_optimized(cores, s)
+    if geom[0] > json.loads(fn.describe())["pieces"]:
+        pytest.skip("more CTAs per cluster than ring pieces")
+    assert fn.tiling(T)["kernel"] == abi.KERNEL_DECODE
+    x = kspec.baseline_x(s, T, seed=7 + T, dtype=dtype, device=DEV)
+    CL, NOC = geom
+    y1 = fn.call_tiled(x, abi.KERNEL_DECODE, T, CL, NOC)
+    y2 = fn.call_tiled(x, abi.KERNEL_DECODE, T, CL, NOC)
+    ref = oracle.tr_forward_reference(x.float().cpu().numpy(),
+                                      [c.float().cpu().numpy() for c in cores])
+    check_close(y1, ref, dtype)
+    torch.testing.assert_close(y1, y2, rtol=0, atol=0)
+    if geom == (0, 0):  # the fused residual add on the same path
+        h = torch.randn(y1.shape, generator=torch.Generator().manual_seed(T)).to(DEV, dtype)
+        add = fn.call_epilogue(x, abi.TR_EPI_ADD, h, False, abi.KERNEL_DECODE)
+        y32 = fn.call_epilogue(x, abi.TR_EPI_NONE, None, True, abi.KERNEL_DECODE)
+        torch.testing.assert_close(y32.to(dtype), y1, rtol=0, atol=0)
+        torch.testing.assert_close(add, (h.float() + y32).to(dtype), rtol=0, atol=0)
+
+
+def test_decode_rejects_three_row_tiles():
+    s = kspec.SPEC_C1
+    fn = prepare_optimized(kspec.baseline_cores(s, device=DEV), s)
+    x = kspec.baseline_x(s, 4, device=DEV)  # 4 tokens x 10 rows (t, o1) > 32
+    with pytest.raises(RuntimeError):
+        fn.call_tiled(x, abi.KERNEL_DECODE, 4, 0, 0)
 
 
 @pytest.mark.parametrize("name", ["c3", "c5", "c4_q", "c4_k", "c4_gate", "c4_down"])

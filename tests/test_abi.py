@@ -140,6 +140,19 @@ def test_geometry_and_workspace():
         p.workspace_bytes(1, too_many)
 
 
+def test_decode_kernel_only_within_two_row_tiles():
+    """The decode kernel serves T while T*O1 <= 32 and T*I2 <= 32 (two m16 tiles of S2 and S1
+    rows); beyond that the tcgen05 kernel (config-4 k at T = 3: 48 S1 rows; down at T = 2: 56)."""
+    cases = {(kspec.SPEC_C4["k"], 2): abi.KERNEL_DECODE, (kspec.SPEC_C4["k"], 3): abi.KERNEL_TC05,
+             (kspec.SPEC_C4["down"], 1): abi.KERNEL_DECODE,
+             (kspec.SPEC_C4["down"], 2): abi.KERNEL_TC05,
+             (kspec.SPEC_C4["q"], 2): abi.KERNEL_DECODE, (kspec.SPEC_C2, 3): abi.KERNEL_DECODE,
+             (kspec.SPEC_C2, 4): abi.KERNEL_TC05}
+    for (s, T), kind in cases.items():
+        p = abi.Plan(s.input_modes, s.output_modes, s.rank, abi.TR_BF16)
+        assert p.tiling(T).kernel == kind, (s, T)
+
+
 # clusters of 1/2/4/8/16 CTAs co-resident on a B200 (the planner's table without a device)
 B200_CLUSTERS = {1: 148, 2: 74, 4: 33, 8: 15, 16: 7}
 

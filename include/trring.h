@@ -70,7 +70,7 @@ typedef struct tr_spec {
  *   cluster         : CTAs per thread-block cluster that share one partial sum in DSMEM
  *   clusters        : clusters per row tile (>1 adds the workspace slot reduction)
  *   kernel          : 0 auto, 1 generic CUDA-core kernel, 2 mma.sync fused tile kernel,
- *                     3 tcgen05 fused kernel, 4 mma.sync decode kernel (T*o1 <= 16; here
+ *                     3 tcgen05 fused kernel, 4 mma.sync decode kernel (T*o1 and T*i2 <= 32; here
  *                     `cluster` splits the pieces and `clusters` the output modes),
  *                     5 tcgen05 small-T kernel (T*o1 <= 128; cores on the MMA's M side)     */
 typedef struct tr_tiling {

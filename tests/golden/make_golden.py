@@ -2,8 +2,8 @@
 
     python tests/golden/make_golden.py [--reference-src PATH]
 
-PATH is the reference's src/ directory (package factorized_inference); default
-$REFERENCE_SRC or /root/reference/src.  Every expected output here comes from the reference's
+PATH is the reference's src/ directory (package factorized_inference); without the flag the
+script reads $REFERENCE_SRC.  Every expected output here comes from the reference's
 own functions: make_cores (reference.py:53-77), tr_forward_reference (reference.py:99-125) and
 the dense fp64 oracle of its tests (tests/test_correctness.py:12-14).  Inputs are drawn on the
 CPU generator so any machine reproduces them.  The files are small and committed; this script
@@ -31,9 +31,10 @@ def sha(t: torch.Tensor) -> str:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-src", default=os.environ.get("REFERENCE_SRC",
-                                                              "/root/reference/src"))
+    ap.add_argument("--reference-src", default=os.environ.get("REFERENCE_SRC"))
     args = ap.parse_args()
+    if not args.reference_src:
+        ap.error("give --reference-src or set REFERENCE_SRC to the reference's src/ directory")
     sys.path.insert(0, args.reference_src)
     sys.path.insert(0, str(ROOT))
     import factorized_inference as ref  # the reference package

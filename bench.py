@@ -1,26 +1,38 @@
 """Benchmark of the tensor-ring operator on B200 -- one JSON line on rank 0.
 
-Workload (BASELINE metric): CUDA-event microseconds per call of the fused operator on the
-1920->2880 ring, modes (8,12,20)->(12,10,24), fp16, at R=8 with T=1/8/32 and at R=16 with
-T=1/32, next to cuBLAS dense fp16 GEMM of the same (d_in, d_out).  Synthetic, seeded: cores
-N(0, sigma^2) with sigma = (R*d_in^(1/3))^(-1/2), x ~ N(0,1).
+Headline workload: CUDA-event microseconds per call of the fused operator on the 1920->2880
+ring, modes (8,12,20)->(12,10,24), fp16, at R=8 with T=1/8/32 and at R=16 with T=1/32, next to
+cuBLAS dense fp16 GEMM of the same (d_in, d_out) and to the reference's own GPU kernels.
+Synthetic, seeded: cores N(0, sigma^2) with sigma = (R*d_in^(1/3))^(-1/2), x ~ N(0,1).
 
 Per case:
-  value leg   one call per step, L2 flushed (256 MiB write) before every step, CUDA events
-              around the call on the launching stream: device time of a cold-cache call.
-  warm leg    the reference harness's protocol: 5 blocks x 20 back-to-back calls, median
-              (benchmarks/benchmark.py:163-174), reported beside the H100 figures.
-  e2e leg     the public API end to end: pinned host x -> device, fn(x), y -> pinned host,
-              after an L2 flush and with the GPU idle, so host dispatch is inside the region.
-  dense bar   F.linear(x, W) on the materialised fp16 W, same legs (TF32 off).
-Extra objects on the line: sharded_prefill (config 5, token-sharded over the ranks) and
-decode_chain (config 4: a T=1 decode step through several layers, fused consumers vs the
-reference's separate consumer launches vs dense bf16; see decode_chain_leg).
+  value leg     one call per step, L2 flushed (256 MiB write) before every step, CUDA events
+                around the call on the launching stream: device time of a cold-cache call.
+  warm leg      the reference harness's protocol: 5 blocks x 20 back-to-back calls, median
+                (benchmarks/benchmark.py:163-174).
+  e2e leg       the public API end to end: pinned host x -> device, fn(x), y -> pinned host,
+                after an L2 flush and with the GPU idle, so host dispatch is inside the region.
+  dense bar     F.linear(x, W) on the materialised fp16 W, same legs (TF32 off).
+  reference     the reference's own PreparedTRKernel (its tr_ring.cu built for sm_100 by
+                baseline/build_reference.py) in a child process: default dispatch, and with the
+                V3 tiling forced at T=1 (TR_KC/TR_QC/TR_TT; its tuned table applies to sm_90
+                only, tr_kernel.py:134-139); and its factorized torch path on the GPU.
+Extra objects on the line:
+  config3          4096->14336 (16,16,16)->(16,28,32) R32 bf16 at T=1/8/32/128/256: ours, dense
+                   bf16 and fp16, the reference's generic kernel;
+  sharded_prefill  config 5, token-sharded over the ranks;
+  decode_chain     config 4: a T=1 decode step through several layers, fused consumers vs the
+                   reference's separate consumer launches vs dense bf16;
+  c1_chain         1920->2880->1920 up/down layers at R8, T=1: per-layer time from stream
+                   launches and from a CUDA graph, against dense fp16 (the launch share a
+                   persistent multi-layer kernel could remove);
+  cpu_baseline     the reference's CPU contraction at 1 thread and at all host threads.
 value = mean over the five cases of the mean value-leg time (the device timer on this part ticks
 in ~2 us steps, so single-call medians are quantised; means over the steps are not).
-ms_per_step = one call of each case.  --impl reference times the reference's CPU path (the numpy restatement in oracle/) on the
+ms_per_step = one call of each case.  --impl reference times the reference's CPU path on the
 host cores instead.  Under torchrun (N>1) every rank serves its own replica of the suite
 (tokens are independent, no collective on the data path); times are the max over ranks.
+--profile-case runs one seeded operator a few times for a profiler (see profiles/).
 """
 from __future__ import annotations
 
@@ -41,11 +53,20 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = ("CUDA-event µs/call at T=1/8/32 (r8), T=1/32 (r16) vs cuBLAS dense fp16 GEMM")
+WORKLOAD = ("c1+c2 decode suite: 1920->2880 (8,12,20)->(12,10,24), R8 T=1/8/32 and R16 "
+            "T=1/32, fp16 (CPU legs fp32)")
 CASES = [(8, 1), (8, 8), (8, 32), (16, 1), (16, 32)]
+C3_TOKENS = (1, 8, 32, 128, 256)
 H100_PUBLISHED = {(8, 1): 8.2, (8, 8): 12.3, (8, 32): 27.9, (16, 1): 10.7, (16, 32): 82.4}
 FLUSH_BYTES = 256 << 20
 KERNEL_NAMES = {1: "ring_generic_kernel", 2: "ring_mma_kernel", 3: "ring_tc05_kernel",
-                4: "ring_decode_kernel"}
+                4: "ring_decode_kernel", 5: "ring_slab_kernel"}
+# the reference install (baseline/build_reference.py); absent -> those legs report why
+REF_SITE = ROOT / "baseline" / "_ref" / "site"
+REF_EXT = ROOT / "baseline" / "_ref" / "tree" / "build" / "tr_ring_ext" / "tr_ring_ext.so"
+# the V3 tilings of the reference's published T=1 runs, forced (BASELINE: H100_TUNED values)
+REF_FORCED = {8: {"TR_KC": "2", "TR_QC": "4", "TR_TT": "1"},
+              16: {"TR_KC": "4", "TR_QC": "4", "TR_TT": "1"}}
 
 
 def parse():
@@ -55,11 +76,27 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-dense", action="store_true")
+    ap.add_argument("--no-reference-kernels", action="store_true",
+                    help="skip the reference's GPU kernels (child processes)")
     ap.add_argument("--chain-layers", type=int, default=4,
                     help="layers of the config-4 decode chain leg (0 = skip)")
     ap.add_argument("--prefill-tokens", type=int, default=65536,
                     help="tokens of the sharded prefill leg (config 5), split over the ranks; "
                          "0 skips it")
+    ap.add_argument("--c3-tokens", default=",".join(map(str, C3_TOKENS)),
+                    help="token counts of the config-3 leg ('' skips it)")
+    # internal: one leg of the reference's GPU code in a child process
+    ap.add_argument("--ref-child", choices=("default", "forced", "torch"), default=None,
+                    help=argparse.SUPPRESS)
+    # --profile-case: one seeded operator, a few calls (for ncu)
+    ap.add_argument("--profile-case", action="store_true")
+    ap.add_argument("--rank", type=int, default=8)
+    ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--input-modes", default="8,12,20")
+    ap.add_argument("--output-modes", default="12,10,24")
+    ap.add_argument("--dtype", default="float16", choices=("float16", "bfloat16", "float32"))
+    ap.add_argument("--calls", type=int, default=5)
+    ap.add_argument("--tiling", default=None, help="kernel,TT,CL,NC forced geometry")
     return ap.parse_args()
 
 
@@ -74,8 +111,9 @@ def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
-    return 6650.0, 1590.0, "fallback"
+        return (d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0),
+                d.get("bf16_tflops_sustained", 1400.0), "measured")
+    return 6650.0, 1590.0, 1400.0, "fallback"
 
 
 class Clocks:
@@ -216,51 +254,258 @@ def max_over_ranks(vals, world):
     return t.tolist()
 
 
-def cpu_reference_leg(steps_budget_s=2.0):
-    """The reference's CPU contraction (numpy restatement, fp32, all host threads) per case."""
+def rel_frob(y, ref):
+    import numpy as np
+
+    y = y.double().cpu().numpy() if isinstance(y, torch.Tensor) else y
+    ref = ref.double().cpu().numpy() if isinstance(ref, torch.Tensor) else ref
+    return float(np.linalg.norm(y - ref) / np.linalg.norm(ref))
+
+
+def reference_rows_check(x, y, cores, spec, rows):
+    """Relative Frobenius error of rows `rows` of y against the reference's own CPU contraction
+    (fp32, from the install in baseline/_ref); None when the reference is not installed."""
+    if not (REF_SITE / "factorized_inference" / "reference.py").exists():
+        return None
+    run, _, _ = reference_cpu_forward()
+    with torch.inference_mode():
+        ref = run(x[rows].float().cpu(), [c.float().cpu() for c in cores], spec)
+    return float(f"{rel_frob(y[rows], ref):.3g}")
+
+
+# ------------------------------------------------------------------------- the CPU baseline
+def cpu_info() -> dict:
+    model = platform.processor() or platform.machine()
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"cpu_model": model, "cpu_count": os.cpu_count()}
+
+
+def reference_cpu_forward():
+    """The reference's own factorized contraction on the CPU (tr_forward_reference,
+    reference.py:99-125, torch fp32) from the install in baseline/_ref; without the install,
+    the numpy restatement in oracle/ (same three contractions, same order)."""
+    if (REF_SITE / "factorized_inference" / "reference.py").exists():
+        if str(REF_SITE) not in sys.path:
+            sys.path.insert(0, str(REF_SITE))
+        from factorized_inference.reference import TRSpec as RefSpec
+        from factorized_inference.reference import tr_forward_reference
+
+        def run(x, cores, spec):
+            return tr_forward_reference(x, cores, RefSpec(spec.input_modes, spec.output_modes,
+                                                          spec.rank))
+        return run, "reference", "tr_forward_reference (reference.py:99-125), torch fp32"
     import oracle
+
+    def run(x, cores, spec):
+        return oracle.tr_forward_reference(x.numpy(), [c.numpy() for c in cores])
+    return run, "port", "numpy restatement of tr_forward_reference (oracle/), fp32"
+
+
+def cpu_leg(threads: int, warm: int = 3, samples: int = 20):
+    """The reference's CPU contraction per case with `threads` host threads: 3 warm-up calls,
+    then the median of `samples` perf_counter samples (the harness protocol)."""
+    from threadpoolctl import threadpool_limits
+
     from kernel_task_b200.spec import TRSpec, baseline_cores, baseline_x
 
-    threads = os.cpu_count() or 1
+    run, kind, what = reference_cpu_forward()
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
     per_case = {}
-    for R, T in CASES:
-        spec = TRSpec((8, 12, 20), (12, 10, 24), R)
-        cores = [c.float().numpy() for c in baseline_cores(spec, seed=0)]
-        x = baseline_x(spec, T, seed=0).float().numpy()
-        oracle.tr_forward_reference(x, cores)
-        lat, t_end = [], time.perf_counter() + steps_budget_s
-        while time.perf_counter() < t_end or len(lat) < 3:
-            t0 = time.perf_counter()
-            oracle.tr_forward_reference(x, cores)
-            lat.append((time.perf_counter() - t0) * 1e6)
-        per_case[f"r{R}_t{T}"] = {"us": statistics.median(lat), "calls": len(lat)}
-    value = statistics.mean(v["us"] for v in per_case.values())
-    return value, threads, per_case
+    try:
+        with threadpool_limits(limits=threads):
+            for R, T in CASES:
+                spec = TRSpec((8, 12, 20), (12, 10, 24), R)
+                cores = [c.float() for c in baseline_cores(spec, seed=0, dtype=torch.float32)]
+                x = baseline_x(spec, T, seed=0, dtype=torch.float32)
+                with torch.inference_mode():
+                    for _ in range(warm):
+                        run(x, cores, spec)
+                    lat = []
+                    for _ in range(samples):
+                        t0 = time.perf_counter()
+                        run(x, cores, spec)
+                        lat.append((time.perf_counter() - t0) * 1e6)
+                per_case[f"r{R}_t{T}"] = round(statistics.median(lat), 2)
+    finally:
+        torch.set_num_threads(prev)
+    return statistics.mean(per_case.values()), per_case, kind, what
+
+
+def cpu_baseline_object():
+    threads = os.cpu_count() or 1
+    v_all, cases_all, kind, what = cpu_leg(threads)
+    v_one, cases_one, _, _ = cpu_leg(1)
+    return {"value": round(v_all, 2), "unit": "us/call", "cores": threads, "kind": kind,
+            "sample": f"{what}; each of the 5 suite cases, 3 warm-up calls then the median of "
+                      "20 calls; value = mean over the cases at all host threads",
+            "cases": cases_all,
+            "one_thread": {"value": round(v_one, 2), "cores": 1, "cases": cases_one},
+            **cpu_info()}
 
 
 def run_reference(args, rank):
+    """--impl reference: the reference's CPU path on the host cores (rank 0 only)."""
     if rank != 0:
         return
-    value, threads, per_case = cpu_reference_leg()
+    threads = os.cpu_count() or 1
+    run, kind, what = reference_cpu_forward()
+    from threadpoolctl import threadpool_limits
+
+    from kernel_task_b200.spec import TRSpec, baseline_cores, baseline_x
+
+    torch.set_num_threads(threads)
+    per_case = {}
+    with threadpool_limits(limits=threads), torch.inference_mode():
+        for R, T in CASES:
+            spec = TRSpec((8, 12, 20), (12, 10, 24), R)
+            cores = [c.float() for c in baseline_cores(spec, seed=0, dtype=torch.float32)]
+            x = baseline_x(spec, T, seed=0, dtype=torch.float32)
+            for _ in range(max(1, args.warmup)):
+                run(x, cores, spec)
+            lat, t_end = [], time.perf_counter() + 2.0
+            while len(lat) < max(3, min(args.steps, 20)) or (time.perf_counter() < t_end
+                                                              and len(lat) < args.steps):
+                t0 = time.perf_counter()
+                run(x, cores, spec)
+                lat.append((time.perf_counter() - t0) * 1e6)
+            per_case[f"r{R}_t{T}"] = {"us": round(statistics.median(lat), 2), "calls": len(lat)}
+    value = statistics.mean(v["us"] for v in per_case.values())
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "us/call",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(sum(v["us"] for v in per_case.values()) / 1e3, 4),
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,sigma^2) cores, N(0,1) x)",
-        "config": {"workload": "c1+c2 decode suite: 1920->2880 (8,12,20)->(12,10,24), "
-                               "R8 T=1/8/32 and R16 T=1/32", "cases": per_case},
+        "config": {"workload": WORKLOAD, "cases": per_case},
         "cpu_baseline": {"value": round(value, 2), "unit": "us/call", "cores": threads,
-                         "kind": "port", "sample": "each of the 5 cases, repeated calls for "
-                         "~2 s, median; numpy fp32 restatement of tr_forward_reference"},
+                         "kind": kind, "sample": f"{what}; each of the 5 suite cases, median "
+                         "of repeated calls (at least 3, up to the step count within ~2 s)"},
         "e2e": {"value": round(value, 2), "unit": "us/call", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-        "cpu": platform.processor() or platform.machine(),
+        **cpu_info(),
     }
     print(json.dumps(line), flush=True)
 
 
-def prefill_leg(args, rank, world, dev, tc_peak):
+# ------------------------------------------------------- the reference's GPU code (children)
+def _load_reference_gpu():
+    """The reference package from baseline/_ref with its prebuilt extension preloaded into
+    tr_kernel._ext (the module load_extension would JIT-build; tr_kernel.py:34-54)."""
+    import importlib.machinery
+    import importlib.util
+
+    if not REF_EXT.exists() or not (REF_SITE / "factorized_inference").exists():
+        raise RuntimeError("reference not installed: run baseline/build_reference.py")
+    sys.path.insert(0, str(REF_SITE))
+    loader = importlib.machinery.ExtensionFileLoader("tr_ring_ext", str(REF_EXT))
+    spec = importlib.util.spec_from_file_location("tr_ring_ext", str(REF_EXT), loader=loader)
+    mod = importlib.util.module_from_spec(spec)
+    loader.exec_module(mod)
+    import factorized_inference.tr_kernel as trk
+
+    trk._ext = mod
+    from factorized_inference import reference, submission
+
+    return submission, reference
+
+
+def ref_child(args):
+    """One child-process leg of the reference's GPU code; prints one JSON line.
+      default  PreparedTRKernel through submission.prepare_optimized, c1/c2 fp16 and c3 bf16
+      forced   the same at T=1 with the V3 tiling forced (TR_KC/TR_QC/TR_TT)
+      torch    tr_forward_reference on the GPU (its torch einsum path), same cases"""
+    import warnings
+
+    from kernel_task_b200.spec import SPEC_C3, TRSpec, baseline_cores, baseline_x
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    try:
+        submission, reference = _load_reference_gpu()
+    except Exception as e:  # noqa: BLE001 -- reported on the line
+        print(json.dumps({"unavailable": str(e)[:300]}), flush=True)
+        return
+    cases = [(f"r{R}_t{T}", TRSpec((8, 12, 20), (12, 10, 24), R), T, torch.float16)
+             for R, T in CASES]
+    cases += [(f"c3_t{T}", SPEC_C3, T, torch.bfloat16) for T in C3_TOKENS]
+    if args.ref_child == "forced":
+        cases = [c for c in cases if c[2] == 1 and c[0].startswith("r")]
+    out = {}
+    for name, spec, T, dtype in cases:
+        rspec = reference.TRSpec(spec.input_modes, spec.output_modes, spec.rank)
+        cores = baseline_cores(spec, seed=0, dtype=dtype, device=dev)
+        x = baseline_x(spec, T, seed=0, dtype=dtype, device=dev)
+        env_prev = {}
+        if args.ref_child == "forced":
+            for k, v in REF_FORCED[spec.rank].items():
+                env_prev[k] = os.environ.get(k)
+                os.environ[k] = v
+        rec = {}
+        try:
+            with warnings.catch_warnings(record=True) as w:
+                warnings.simplefilter("always")
+                if args.ref_child == "torch":
+                    fn = lambda v, c=cores, s=rspec: reference.tr_forward_reference(v, c, s)  # noqa
+                else:
+                    fn = submission.prepare_optimized(cores, rspec)
+                with torch.inference_mode():
+                    y = fn(x)
+                    torch.cuda.synchronize()
+                    big = T > 32
+                    steps = 3 if big else min(args.steps, 20)
+                    rec["us"] = round(statistics.mean(cold_device_us(fn, x, flush, steps, 2)), 3)
+                    if not big:
+                        rec["warm_stream_us"] = round(warm_stream_us(fn, x), 3)
+                rec["fallback_warnings"] = [str(m.message)[:120] for m in w][:2]
+            rec["rel_frob"] = reference_rows_check(x, y, cores, spec, list(range(min(T, 4))))
+            if args.ref_child != "torch":
+                rec["tiling"] = list(fn._tiling.get(T) or ()) if hasattr(fn, "_tiling") else None
+        except Exception as e:  # noqa: BLE001 -- one failing case does not hide the others
+            rec = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+        finally:
+            for k, v in env_prev.items():
+                if v is None:
+                    os.environ.pop(k, None)
+                else:
+                    os.environ[k] = v
+        out[name] = rec
+        del cores, x
+        torch.cuda.empty_cache()
+    print(json.dumps({"mode": args.ref_child, "cases": out}), flush=True)
+
+
+def reference_gpu_legs(args) -> dict:
+    """Runs each leg of the reference's GPU code in its own child process, so that the
+    reference's extension never maps into the process that runs this library's kernels (as its
+    harness isolates each method, benchmarks/benchmark.py:263-283)."""
+    if not REF_EXT.exists():
+        return {"unavailable": "reference extension not built (baseline/build_reference.py)"}
+    res = {}
+    for mode in ("default", "forced", "torch"):
+        cmd = [sys.executable, str(ROOT / "bench.py"), "--ref-child", mode,
+               "--steps", str(args.steps)]
+        try:
+            p = subprocess.run(cmd, capture_output=True, text=True, timeout=900, cwd=str(ROOT))
+            lines = [ln for ln in p.stdout.splitlines() if ln.startswith("{")]
+            res[mode] = json.loads(lines[-1]) if lines else {
+                "error": f"rc={p.returncode}: {p.stderr.strip()[-300:]}"}
+        except subprocess.TimeoutExpired:
+            res[mode] = {"error": "timed out after 900 s"}
+    return res
+
+
+# ---------------------------------------------------------------------- the extra legs
+def prefill_leg(args, rank, world, dev, tc_peak, tc_sustained):
     """Config 5: 4096 -> 14336, modes (16,16,16)->(16,28,32), R16, bf16, `--prefill-tokens`
     tokens split over the ranks (ShardedRing row split, cores replicated, no collective on the
     data path).  Device time per call (CUDA events), max over ranks; one all_gather of y timed
@@ -295,10 +540,18 @@ def prefill_leg(args, rank, world, dev, tc_peak):
                        "cores replicated per GPU",
            "tokens": T, "tokens_per_rank_max": shard_bounds(T, world, 0)[1],
            "ms": round(ms, 3), "tokens_per_s": round(T / (ms * 1e-3), 1),
-           "steps": steps, "scaling": "strong", "timing": "CUDA events, max over ranks"}
+           "steps": steps, "scaling": "strong", "timing": "CUDA events, max over ranks",
+           "kernel": KERNEL_NAMES.get(op.fn.tiling(b - a)["kernel"], "?"),
+           "tiling": op.fn.tiling(b - a)}
     flops = op.fn.flops_per_token() * shard_bounds(T, world, 0)[1]
-    out["tflops_per_gpu"] = round(flops / (ms * 1e-3) / 1e12, 2)
-    out["frac_of_peak"] = round(flops / (ms * 1e-3) / 1e12 / tc_peak, 4)
+    tf = flops / (ms * 1e-3) / 1e12
+    out["tflops_per_gpu"] = round(tf, 2)
+    out["frac_of_peak"] = round(tf / tc_peak, 4)
+    out["frac_of_sustained_peak"] = round(tf / tc_sustained, 4)
+    # parity at full size: sampled rows of rank 0's shard against the reference's CPU path
+    if rank == 0:
+        out["sampled_rows_rel_frob"] = reference_rows_check(
+            x, y, cores, SPEC_C5, [0, (b - a) // 3, (b - a) - 1])
     if world > 1:
         rows_max = shard_bounds(T, world, 0)[1]
         padded = y.new_zeros((rows_max, SPEC_C5.out_features))
@@ -313,6 +566,39 @@ def prefill_leg(args, rank, world, dev, tc_peak):
         out["gather_ms"] = round(max_over_ranks([e0.elapsed_time(e1)], world)[0], 3)
         del parts, padded
     del x, y, op
+    torch.cuda.empty_cache()
+    return out
+
+
+def c3_leg(dev, flush, tokens, tc_peak, dense=True):
+    """Config 3: 4096 -> 14336, modes (16,16,16)->(16,28,32), R32, bf16 (seeded BASELINE
+    inputs): cold device time per call (L2 flushed), our kernel and the dense bars."""
+    from kernel_task_b200 import prepare_optimized
+    from kernel_task_b200.spec import SPEC_C3, baseline_cores, baseline_x
+
+    cores = baseline_cores(SPEC_C3, seed=0, dtype=torch.bfloat16, device=dev)
+    fn = prepare_optimized(cores, SPEC_C3)
+    W16 = Wb = None
+    if dense:
+        Wb = dense_weight(cores)
+        W16 = Wb.to(torch.float16)
+    out = {"workload": "c3: 4096->14336 (16,16,16)->(16,28,32) R32 bf16", "cases": {}}
+    for T in tokens:
+        x = baseline_x(SPEC_C3, T, seed=0, dtype=torch.bfloat16, device=dev)
+        steps = 3 if T >= 128 else 10
+        us = statistics.mean(cold_device_us(fn, x, flush, steps, 2))
+        flops = fn.flops_per_token() * T
+        rec = {"us": round(us, 3), "kernel": KERNEL_NAMES.get(fn.tiling(T)["kernel"], "?"),
+               "tiling": fn.tiling(T), "tflops": round(flops / (us * 1e-6) / 1e12, 2),
+               "frac_of_peak": round(flops / (us * 1e-6) / 1e12 / tc_peak, 4)}
+        if dense:
+            x16 = x.to(torch.float16)
+            rec["dense_bf16_us"] = round(statistics.mean(cold_device_us(
+                lambda v: torch.nn.functional.linear(v, Wb), x, flush, steps, 2)), 3)
+            rec["dense_fp16_us"] = round(statistics.mean(cold_device_us(
+                lambda v: torch.nn.functional.linear(v, W16), x16, flush, steps, 2)), 3)
+        out["cases"][f"t{T}"] = rec
+    del fn, W16, Wb
     torch.cuda.empty_cache()
     return out
 
@@ -383,26 +669,83 @@ def decode_chain_leg(dev, layers, T=1):
     out["fused_vs_unfused_rel_frob"] = float(f"{rel:.3g}")
     for name, fn in (("fused", fused), ("unfused", unfused), ("dense_bf16", dense)):
         out[f"{name}_us_per_layer"] = round(warm_stream_us(fn, h0, 5, 10) / layers, 3)
-    try:
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            for _ in range(3):
-                fused(h0)
-        torch.cuda.current_stream().wait_stream(s)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            fused(h0)
+    graph = _graph_of(fused, h0)
+    if isinstance(graph, str):
+        out["fused_graph_error"] = graph
+    else:
         out["fused_graph_us_per_layer"] = round(
             warm_stream_us(lambda _: graph.replay(), None, 5, 10) / layers, 3)
         del graph
-    except RuntimeError as e:  # report, keep the rest of the line
-        out["fused_graph_error"] = str(e).splitlines()[0][:200]
     del L, Ws
     torch.cuda.empty_cache()
     return out
 
 
+def _graph_of(fn, arg):
+    """CUDA graph of fn(arg) (warmed on a side stream), or an error string."""
+    try:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                fn(arg)
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn(arg)
+        return graph
+    except RuntimeError as e:
+        return str(e).splitlines()[0][:200]
+
+
+def c1_chain_leg(dev, layers=16):
+    """The reference's comparison point for a persistent multi-layer kernel: a chain of
+    1920->2880 (up) and 2880->1920 (down) R8 fp16 layers at T=1 (kernel_work/stack,
+    REPORT_TEMPLATE.md:307-310).  Microseconds per layer, warm: stream launches, CUDA-graph
+    replay, and dense fp16 cuBLAS both ways; the empty-kernel floor for scale."""
+    import torch.nn.functional as F
+
+    from kernel_task_b200 import prepare_optimized
+    from kernel_task_b200._native import binding
+    from kernel_task_b200.spec import TRSpec, baseline_cores, baseline_x
+
+    up, down = TRSpec((8, 12, 20), (12, 10, 24), 8), TRSpec((12, 10, 24), (8, 12, 20), 8)
+    specs = [(up, down)[l % 2] for l in range(layers)]
+    cores = [baseline_cores(s, seed=200 + l, dtype=torch.float16, device=dev)
+             for l, s in enumerate(specs)]
+    ops = [prepare_optimized(c, s) for c, s in zip(cores, specs)]
+    Ws = [dense_weight(c) for c in cores]
+    h0 = baseline_x(up, 1, seed=3, dtype=torch.float16, device=dev)
+
+    def ring(h):
+        for op in ops:
+            h = op(h)
+        return h
+
+    def dense(h):
+        for W in Ws:
+            h = F.linear(h, W)
+        return h
+
+    empty = binding().empty_launch
+    out = {"workload": f"{layers} alternating 1920->2880 / 2880->1920 R8 fp16 layers, T=1",
+           "ring_stream_us_per_layer": round(warm_stream_us(ring, h0, 5, 10) / layers, 3),
+           "dense_stream_us_per_layer": round(warm_stream_us(dense, h0, 5, 10) / layers, 3),
+           "empty_kernel_stream_us": round(warm_stream_us(lambda _: empty(), None), 3)}
+    for name, fn in (("ring", ring), ("dense", dense)):
+        graph = _graph_of(fn, h0)
+        if isinstance(graph, str):
+            out[f"{name}_graph_error"] = graph
+        else:
+            out[f"{name}_graph_us_per_layer"] = round(
+                warm_stream_us(lambda _: graph.replay(), None, 5, 10) / layers, 3)
+            del graph
+    del ops, Ws
+    torch.cuda.empty_cache()
+    return out
+
+
+# ---------------------------------------------------------------------------- our arm
 def run_ours(args, rank, world, local_rank):
     from kernel_task_b200 import prepare_optimized
     from kernel_task_b200.spec import TRSpec, baseline_cores, baseline_x
@@ -412,7 +755,7 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
-    hbm_peak, tc_peak, peak_kind = peaks()
+    hbm_peak, tc_peak, tc_sustained, peak_kind = peaks()
     steps, warmup = args.steps, max(3, args.warmup)
 
     cases = {}
@@ -474,17 +817,24 @@ def run_ours(args, rank, world, local_rank):
     empty = binding().empty_launch
     launch_cold = statistics.mean(cold_device_us(lambda _v: empty(), None, flush, steps, warmup))
     launch_warm = warm_stream_us(lambda _v: empty(), None)
-    prefill = (prefill_leg(args, rank, world, dev, tc_peak) if args.prefill_tokens > 0
-               else None)
+    c3_tokens = [int(v) for v in args.c3_tokens.split(",") if v.strip()]
+    c3 = (c3_leg(dev, flush, c3_tokens, tc_peak, dense=not args.no_dense)
+          if c3_tokens and world == 1 else None)
+    prefill = (prefill_leg(args, rank, world, dev, tc_peak, tc_sustained)
+               if args.prefill_tokens > 0 else None)
     chain = (decode_chain_leg(dev, args.chain_layers)
              if args.chain_layers > 0 and world == 1 else None)
-    clk = clocks.stop()  # sampled from before the cold legs to the end of the chain leg
+    c1_chain = c1_chain_leg(dev) if world == 1 and args.chain_layers > 0 else None
+    clk = clocks.stop()  # sampled from before the cold legs to the end of the chain legs
     keys = list(cases)
     med = max_over_ranks([statistics.median(cases[k]["cold"]) for k in keys], world)
     mean = max_over_ranks([statistics.mean(cases[k]["cold"]) for k in keys], world)
     e2e = max_over_ranks([statistics.mean(cases[k]["e2e"]) for k in keys], world)
     if rank != 0:
         return
+    # the reference's GPU code, in child processes (after our legs, GPU otherwise idle)
+    ref_gpu = (reference_gpu_legs(args) if world == 1 and not args.no_reference_kernels
+               else None)
     # binding floor per case: max(launch floor, compulsory bytes / HBM, FLOPs / tensor peak)
     floors, warm_floors = [], []
     for k in keys:
@@ -499,11 +849,13 @@ def run_ours(args, rank, world, local_rank):
         c = cases[k]
         R, T = k
         spec = c["spec"]
+        name = f"r{R}_t{T}"
         bytes_min = 2 * (spec.factor_parameters + T * (spec.in_features + spec.out_features))
-        per_case[f"r{R}_t{T}"] = {
+        rec = {
             "us": round(mean[i], 3), "us_median": round(med[i], 3),
             "warm_stream_us": round(c["warm"], 3), "host_latency_us": round(c["host"], 2),
             "e2e_us": round(e2e[i], 3), "prep_ms": round(c["prep_ms"], 2),
+            "kernel": KERNEL_NAMES.get(c["tiling"]["kernel"], "?"),
             "dense_us": round(c.get("dense_cold", float("nan")), 3),
             "dense_warm_stream_us": round(c.get("dense_warm", float("nan")), 3),
             "dense_e2e_us": round(c.get("dense_e2e", float("nan")), 3),
@@ -518,6 +870,29 @@ def run_ours(args, rank, world, local_rank):
             "warm_floor_us": round(warm_floors[i], 3),
             "warm_frac_of_floor": round(warm_floors[i] / c["warm"], 4),
         }
+        if ref_gpu and "default" in ref_gpu:
+            d = ref_gpu["default"].get("cases", {}).get(name, {})
+            f = ref_gpu.get("forced", {}).get("cases", {}).get(name, {})
+            t = ref_gpu.get("torch", {}).get("cases", {}).get(name, {})
+            legs = [v for v in (d.get("us"), f.get("us")) if v is not None]
+            if legs:
+                rec["ref_kernel_us"] = min(legs)
+                rec["ref_kernel_default_us"] = d.get("us")
+                rec["ref_kernel_forced_us"] = f.get("us")
+                warm = [v for v in (d.get("warm_stream_us"), f.get("warm_stream_us"))
+                        if v is not None]
+                rec["ref_kernel_warm_us"] = min(warm) if warm else None
+                rec["ref_kernel_rel_frob"] = d.get("rel_frob")
+            rec["ref_torch_us"] = t.get("us")
+            rec["ref_torch_warm_us"] = t.get("warm_stream_us")
+        per_case[name] = rec
+    if c3 is not None and ref_gpu and "default" in ref_gpu:
+        for name, rec in c3["cases"].items():
+            d = ref_gpu["default"].get("cases", {}).get(f"c3_{name}", {})
+            t = ref_gpu.get("torch", {}).get("cases", {}).get(f"c3_{name}", {})
+            rec["ref_kernel_us"] = d.get("us", d.get("error"))
+            rec["ref_kernel_rel_frob"] = d.get("rel_frob")
+            rec["ref_torch_us"] = t.get("us", t.get("error"))
     # roofline of the dominant kernel: the case with the largest device time
     dom = max(range(len(keys)), key=lambda i: mean[i])
     dk = keys[dom]
@@ -532,8 +907,7 @@ def run_ours(args, rank, world, local_rank):
         "steps": steps, "warmup": warmup, "ms_per_step": round(sum(mean) / 1e3, 5),
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded N(0,sigma^2) cores, N(0,1) x)",
-        "config": {"workload": "c1+c2 decode suite: 1920->2880 (8,12,20)->(12,10,24), "
-                               "R8 T=1/8/32 and R16 T=1/32, fp16",
+        "config": {"workload": WORKLOAD,
                    "l2": "flushed (256 MiB write) before every timed call",
                    "parallelism": f"replica x{world}" if world > 1 else "single GPU",
                    "cases": per_case},
@@ -551,21 +925,49 @@ def run_ours(args, rank, world, local_rank):
                      "peak_kind": f"{peak_kind} bf16 dense (burst)"},
         "clocks": clk,
     }
+    if c3 is not None:
+        line["config3"] = c3
     if prefill is not None:
         line["sharded_prefill"] = prefill
     if chain is not None:
         line["decode_chain"] = chain
+    if c1_chain is not None:
+        line["c1_chain"] = c1_chain
+    if ref_gpu is not None:
+        line["reference_gpu"] = {m: {k: v for k, v in r.items() if k != "cases"}
+                                 for m, r in ref_gpu.items() if isinstance(r, dict)}
     if world == 1:
-        value_cpu, threads, cpu_cases = cpu_reference_leg(1.0)
-        line["cpu_baseline"] = {"value": round(value_cpu, 2), "unit": "us/call", "cores": threads,
-                                "kind": "port", "sample": "each of the 5 cases, repeated "
-                                "calls for ~1 s, median; numpy fp32 restatement of "
-                                "tr_forward_reference", "cases": cpu_cases}
+        line["cpu_baseline"] = cpu_baseline_object()
     print(json.dumps(line), flush=True)
+
+
+def profile_case(args):
+    """One seeded operator, `--calls` calls, then synchronise: under
+    `ncu -k regex:ring -s <calls-1> -c 1` it captures the last call's kernel."""
+    from kernel_task_b200 import prepare_optimized
+    from kernel_task_b200.spec import TRSpec, baseline_cores, baseline_x
+
+    spec = TRSpec(tuple(int(v) for v in args.input_modes.split(",")),
+                  tuple(int(v) for v in args.output_modes.split(",")), args.rank)
+    dtype = getattr(torch, args.dtype)
+    dev = torch.device("cuda")
+    fn = prepare_optimized(baseline_cores(spec, dtype=dtype, device=dev), spec)
+    x = baseline_x(spec, args.tokens, dtype=dtype, device=dev)
+    forced = tuple(int(v) for v in args.tiling.split(",")) if args.tiling else None
+    for _ in range(args.calls):
+        y = fn.call_tiled(x, *forced) if forced else fn(x)
+    torch.cuda.synchronize()
+    print(f"ok {tuple(y.shape)} tiling={fn.tiling(args.tokens)} {fn.describe()}")
 
 
 def main():
     args = parse()
+    if args.ref_child:
+        ref_child(args)
+        return
+    if args.profile_case:
+        profile_case(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -71,8 +71,7 @@ typedef struct tr_spec {
  *   clusters        : clusters per row tile (>1 adds the workspace slot reduction)
  *   kernel          : 0 auto, 1 generic CUDA-core kernel, 2 mma.sync fused tile kernel,
  *                     3 tcgen05 fused kernel, 4 mma.sync decode kernel (T*o1 and T*i2 <= 32; here
- *                     `cluster` splits the pieces and `clusters` the output modes),
- *                     5 tcgen05 small-T kernel (T*o1 <= 128; cores on the MMA's M side)     */
+ *                     `cluster` splits the pieces and `clusters` the output modes)          */
 typedef struct tr_tiling {
   int32_t tokens_per_tile;
   int32_t cluster;
@@ -107,6 +106,21 @@ int tr_workspace_bytes_tiled(const tr_plan* plan, int64_t tokens, const struct t
                              size_t* bytes);
 int tr_workspace_clear(void* workspace, size_t bytes, void* stream);
 
+/* Device status of the calls that used `workspace`: TR_OK, or TR_ERR_TIMEOUT when a bounded
+ * wait inside a tcgen05 kernel gave up (its y is then not valid).  The kernels record a timeout
+ * in the first workspace word instead of hanging; a forward call returns before its kernel
+ * runs, so only this read (stream-ordered: it synchronises `stream`) can see it.  `reset` != 0
+ * clears the word, which every later call otherwise finds set.  A zero-byte workspace has no
+ * status (the decode and mma kernels have no waits that can expire).  The reference has no
+ * counterpart: its design-B kernels have no bounded waits (csrc/tr_ring.cu:302-337).        */
+int tr_workspace_status(void* workspace, size_t workspace_bytes, int32_t* status, int32_t reset,
+                        void* stream);
+
+/* Polls a bounded device-side wait of this plan's tcgen05 kernels makes before it gives up and
+ * reports TR_ERR_TIMEOUT (0 = built-in limit, about a second).  For tests of the timeout path:
+ * a tiny limit makes the waits expire on a healthy GPU.  No reference counterpart.            */
+int tr_plan_set_wait_limit(tr_plan* plan, uint32_t polls);
+
 /* y[tokens, d_out] = TR(x[tokens, d_in]).  x, y: contiguous row-major, plan dtype, 16-byte
  * aligned.  tokens == 0 is a no-op.  Launches exactly one kernel on `stream`.                 */
 int tr_forward(const tr_plan* plan, const void* packed, const void* x, int64_t tokens, void* y,
@@ -129,7 +143,13 @@ int tr_forward_tiled(const tr_plan* plan, const void* packed, const void* x, int
  * call on a device looks up the array's device address on that device; make that first call
  * before any stream capture.  All calls share the one array and it keeps the last call's
  * contents, so calls whose kernels overlap on the GPU (two streams, two threads) race and give
- * wrong results; issue them in one stream order.  fp16/bf16 plans only.                       */
+ * wrong results; issue them in one stream order.  fp16/bf16 plans only.
+ * The array's device address is looked up once per device and kept for the life of the
+ * process: after cudaDeviceReset, or after the device's primary context is released and
+ * created again, that address is stale, so do not call this entry point after either.
+ * Each call issues two operations on `stream`: a cudaMemsetAsync that zeroes the array's
+ * arrival counters (a guard against an earlier call whose kernel never ran to its end), then
+ * the kernel.                                                                                */
 #define TR_NOALLOC_SCRATCH_BYTES (8u << 20)
 int tr_forward_noalloc(const tr_plan* plan, const void* packed, const void* x, int64_t tokens,
                        void* y, void* stream);

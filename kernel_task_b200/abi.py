@@ -4,7 +4,8 @@ integers (``tensor.data_ptr()``), streams are ``cudaStream_t`` handles as intege
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, c_char_p, c_double, c_int, c_int32, c_int64, c_size_t, c_void_p
+from ctypes import (POINTER, c_char_p, c_double, c_int, c_int32, c_int64, c_size_t,
+                    c_uint32, c_void_p)
 
 from ._native import LIBRARY
 
@@ -16,7 +17,7 @@ TR_ERR_CUDA = -4
 TR_ERR_ALIGN = -5
 TR_ERR_TIMEOUT = -6
 TR_F32, TR_F16, TR_BF16 = 0, 1, 2
-KERNEL_AUTO, KERNEL_GENERIC, KERNEL_MMA, KERNEL_TC05, KERNEL_DECODE, KERNEL_TCS = 0, 1, 2, 3, 4, 5
+KERNEL_AUTO, KERNEL_GENERIC, KERNEL_MMA, KERNEL_TC05, KERNEL_DECODE = 0, 1, 2, 3, 4
 TR_EPI_NONE, TR_EPI_ADD, TR_EPI_SILU_MUL = 0, 1, 2
 
 
@@ -44,6 +45,8 @@ PROTOTYPES = {
     "tr_workspace_bytes_tiled": (c_int, [c_void_p, c_int64, POINTER(TrTiling),
                                          POINTER(c_size_t)]),
     "tr_workspace_clear": (c_int, [c_void_p, c_size_t, c_void_p]),
+    "tr_workspace_status": (c_int, [c_void_p, c_size_t, POINTER(c_int32), c_int32, c_void_p]),
+    "tr_plan_set_wait_limit": (c_int, [c_void_p, c_uint32]),
     "tr_forward": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_size_t,
                            c_void_p]),
     "tr_forward_tiled": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
@@ -90,6 +93,14 @@ class AbiError(RuntimeError):
 def check(status: int, what: str) -> None:
     if status != TR_OK:
         raise AbiError(status, what)
+
+
+def workspace_status(ws_ptr: int, ws_bytes: int, reset: bool = True, stream: int = 0) -> int:
+    """The device status word of a workspace (TR_OK or TR_ERR_TIMEOUT); synchronises `stream`."""
+    st = c_int32()
+    check(lib().tr_workspace_status(c_void_p(ws_ptr or None), ws_bytes, ctypes.byref(st),
+                                    1 if reset else 0, c_void_p(stream)), "tr_workspace_status")
+    return st.value
 
 
 class Plan:
@@ -143,6 +154,10 @@ class Plan:
             self.handle, c_void_p(packed_ptr), c_void_p(x_ptr), tokens, c_void_p(y_ptr),
             ctypes.byref(epilogue) if epilogue else None, c_void_p(ws_ptr or None), ws_bytes,
             ctypes.byref(tiling) if tiling else None, c_void_p(stream))
+
+    def set_wait_limit(self, polls: int) -> None:
+        """Polls of a bounded device-side wait before it gives up (0 = built-in limit)."""
+        check(lib().tr_plan_set_wait_limit(self.handle, polls), "tr_plan_set_wait_limit")
 
     def tiling(self, tokens: int) -> TrTiling:
         t = TrTiling()

@@ -559,104 +559,6 @@ int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* f, TcGeom* g) {
   return TR_OK;
 }
 
-// Small-T tcgen05 geometry (ring_tcs.cu).  Groups of O2G output modes with O2G * RP <= 128
-// (S2's rows) and T * O1 * O2G <= 128 (S3's rows); as many groups per CTA as their G2 blocks
-// fit in shared memory; the pieces of each set of groups split over one wave of clusters.
-int resolve_tcs_geom(const Plan& p, int64_t T, const tr_tiling* f, TcsGeom* g) {
-  const Canon& c = p.c;
-  const MmaLayout& m = p.m;
-  const TcLayout& t = p.t;
-  if (!p.tc_ok) {
-    set_error("tcgen05 kernels do not support this spec/dtype");
-    return TR_ERR_UNSUPPORTED;
-  }
-  const int RP = m.RP;
-  if (T < 1 || T * c.O1 > 128 || T * c.I2 > 256) {
-    set_error("small-T tcgen05 kernel: T=%lld gives %lld S3 rows (t, o1) (at most 128)",
-              (long long)T, (long long)T * c.O1);
-    return TR_ERR_UNSUPPORTED;
-  }
-  g->N1C = ceil_div((int)T * c.I2, 16) * 16;
-  g->N2C = ceil_div((int)T * c.O1, 16) * 16;
-  g->MT1 = ceil_div(t.N1P, 128);
-  int o2g = std::min(std::min(128 / RP, 128 / ((int)T * c.O1)), c.O2);
-  if (o2g < 1 || g->MT1 > 2) {
-    set_error("small-T tcgen05 kernel: no o2 group fits");
-    return TR_ERR_UNSUPPORTED;
-  }
-  g->NG = ceil_div(c.O2, o2g);
-  g->O2G = ceil_div(c.O2, g->NG);  // balanced groups
-  const int K1P = m.K1P, K2P = m.K2P, K3P = t.K3P, N3P = t.N3P;
-  g->a2_stride = (size_t)128 * K2P * 2;
-  g->b1_bytes = (size_t)g->N1C * K1P * 2;
-  g->a1_stride = (size_t)g->MT1 * 128 * K1P * 2;
-  g->b3_stride = (size_t)N3P * K3P * 2;
-  g->b2_bytes = (size_t)g->N2C * K2P * 2;
-  g->a3_stride = (size_t)128 * K3P * 2;
-  g->d1_col = 0;
-  g->d2_col = g->MT1 * g->N1C;
-  auto layout = [&](int ngc, int CL, int NB, int NQ) {
-    const size_t ys = (size_t)ngc * 128 * c.O3 * 4;
-    const size_t sl = (size_t)ceil_div(ngc * 128 * c.O3, CL);
-    const size_t recv = (size_t)CL * sl * 4;
-    g->off_a2 = 0;
-    g->off_ys = 0;
-    g->off_recv = align_up(ys, 128);
-    const size_t region = std::max((size_t)ngc * g->a2_stride, g->off_recv + recv);
-    g->off_b1 = align_up(region, 128);
-    g->off_a1 = align_up(g->off_b1 + (size_t)NQ * g->b1_bytes, 128);
-    g->off_b3 = align_up(g->off_a1 + (size_t)NB * g->a1_stride, 128);
-    g->off_b2 = align_up(g->off_b3 + (size_t)NB * g->b3_stride, 128);
-    g->off_a3 = align_up(g->off_b2 + g->b2_bytes, 128);
-    g->off_bar = align_up(g->off_a3 + (size_t)ngc * g->a3_stride, 128);
-    return g->off_bar + 256 + 1024;  // barriers, TMEM slot, flags; 1024-byte alignment slack
-  };
-  auto tmem_need = [&](int ngc) { return g->d2_col + ngc * (g->N2C + N3P); };
-  // groups per CTA: all of them when their G2 fits (and TMEM), else the most that fit
-  int ngc = std::min(g->NG, 8);
-  while (ngc > 1 && (tmem_need(ngc) > 512 || layout(ngc, 16, 1, 2) > p.smem_optin)) --ngc;
-  if (tmem_need(ngc) > 512 || layout(ngc, 16, 1, 2) > p.smem_optin) {
-    set_error("small-T tcgen05 kernel: one o2 group does not fit");
-    return TR_ERR_UNSUPPORTED;
-  }
-  g->NGC = ngc;
-  g->NGS = ceil_div(g->NG, ngc);
-  int CL, NC;
-  if (f && f->cluster > 0) {
-    CL = f->cluster;
-    NC = f->clusters > 0 ? f->clusters : 1;
-  } else {
-    const int NJ = std::max(1, std::min(p.num_sms / g->NGS, m.npieces));
-    one_wave_split(p, g->NGS, NJ, 16, &CL, &NC);
-  }
-  if (CL < 1 || CL > 16 || NC < 1 || (long long)CL * NC > m.npieces) {
-    set_error("cluster=%d clusters=%d invalid for %d pieces", CL, NC, m.npieces);
-    return TR_ERR_INVALID;
-  }
-  g->CL = CL;
-  g->NC = NC;
-  const int NJ = CL * NC;
-  const int max_np = ceil_div(m.npieces, NJ);
-  g->NQ = std::min(c.I3, ceil_div(max_np, c.R) + 1);
-  int NB = std::min(max_np, 16);
-  while (NB > 1 && layout(ngc, CL, NB, g->NQ) > p.smem_optin) --NB;
-  g->NB = NB;
-  // at least 120 KB, so no two CTAs share an SM (TMEM allocation across cluster barriers)
-  g->smem = std::max<size_t>(layout(ngc, CL, NB, g->NQ), 120 * 1024);
-  if (g->smem > p.smem_optin) {
-    set_error("small-T tcgen05 kernel needs %zu bytes of shared memory", g->smem);
-    return TR_ERR_UNSUPPORTED;
-  }
-  g->d3_col = g->d2_col + ngc * g->N2C;
-  g->tmem_cols = 32;
-  while (g->tmem_cols < tmem_need(ngc)) g->tmem_cols *= 2;
-  g->slot_elems = ngc * 128 * c.O3;
-  const size_t counters = align_up((size_t)g->NGS * CL * sizeof(int), 256);
-  g->ws_bytes = 256 + counters +
-                (NC > 1 ? (size_t)g->NGS * NC * g->slot_elems * sizeof(float) : 0);
-  return TR_OK;
-}
-
 // Which kernel serves `T` tokens on this plan.
 static int pick_kind(const Plan& p, int64_t T, const tr_tiling* f) {
   if (f && f->kernel != KIND_AUTO) return f->kernel;
@@ -687,7 +589,6 @@ struct GeomCacheEntry {
   trr::MmaGeom g;
   trr::DecodeGeom dg;
   trr::TcGeom tg;
-  trr::TcsGeom sg;
 };
 
 struct tr_plan : public trr::Plan {
@@ -815,10 +716,10 @@ int tr_plan_flops_per_token(const tr_plan* plan, double* flops) {
 }
 
 static int resolve_geom(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling, int* kind,
-                        MmaGeom* g, DecodeGeom* dg, TcGeom* tg, TcsGeom* sg);
+                        MmaGeom* g, DecodeGeom* dg, TcGeom* tg);
 
 static int geom_for(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling, int* kind,
-                    MmaGeom* g, DecodeGeom* dg, TcGeom* tg, TcsGeom* sg) {
+                    MmaGeom* g, DecodeGeom* dg, TcGeom* tg) {
   if (!plan) {
     set_error("null plan");
     return TR_ERR_INVALID;
@@ -835,11 +736,10 @@ static int geom_for(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling
       *g = e.g;
       *dg = e.dg;
       *tg = e.tg;
-      *sg = e.sg;
       return TR_OK;
     }
   }
-  const int st = resolve_geom(plan, tokens, tiling, kind, g, dg, tg, sg);
+  const int st = resolve_geom(plan, tokens, tiling, kind, g, dg, tg);
   if (st == TR_OK && !tiling && tokens > 0) {
     std::lock_guard<std::mutex> lock(plan->cache_mu);
     GeomCacheEntry& e = plan->cache[(uint64_t)tokens % 32];
@@ -848,13 +748,12 @@ static int geom_for(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling
     e.g = *g;
     e.dg = *dg;
     e.tg = *tg;
-    e.sg = *sg;
   }
   return st;
 }
 
 static int resolve_geom(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling, int* kind,
-                        MmaGeom* g, DecodeGeom* dg, TcGeom* tg, TcsGeom* sg) {
+                        MmaGeom* g, DecodeGeom* dg, TcGeom* tg) {
   *kind = pick_kind(*plan, tokens, tiling);
   if (*kind == KIND_MMA) {
     if (tokens == 0) {
@@ -878,12 +777,6 @@ static int resolve_geom(const tr_plan* plan, int64_t tokens, const tr_tiling* ti
     if (tokens == 0) return TR_OK;
     return resolve_tc_geom(*plan, tokens, tiling, tg);
   }
-  if (*kind == KIND_TCS) {
-    memset(g, 0, sizeof(*g));
-    memset(sg, 0, sizeof(*sg));
-    if (tokens == 0) return TR_OK;
-    return resolve_tcs_geom(*plan, tokens, tiling, sg);
-  }
   set_error("kernel kind %d not available in this build", *kind);
   return TR_ERR_UNSUPPORTED;
 }
@@ -898,13 +791,9 @@ int tr_workspace_bytes_tiled(const tr_plan* plan, int64_t tokens, const tr_tilin
   MmaGeom g;
   DecodeGeom dg;
   TcGeom tg;
-  TcsGeom sg;
-  const int st = geom_for(plan, tokens, tiling, &kind, &g, &dg, &tg, &sg);
+  const int st = geom_for(plan, tokens, tiling, &kind, &g, &dg, &tg);
   if (st != TR_OK) return st;
-  *bytes = kind == KIND_MMA    ? g.ws_bytes
-           : kind == KIND_TC05 ? tg.ws_bytes
-           : kind == KIND_TCS  ? sg.ws_bytes
-                               : 0;
+  *bytes = kind == KIND_MMA ? g.ws_bytes : kind == KIND_TC05 ? tg.ws_bytes : 0;
   return TR_OK;
 }
 
@@ -926,6 +815,40 @@ int tr_workspace_clear(void* workspace, size_t bytes, void* stream) {
   return TR_OK;
 }
 
+int tr_workspace_status(void* workspace, size_t workspace_bytes, int32_t* status, int32_t reset,
+                        void* stream) {
+  if (!status) {
+    set_error("null status pointer");
+    return TR_ERR_INVALID;
+  }
+  *status = TR_OK;
+  if (workspace_bytes == 0) return TR_OK;  // the kernels of this token count keep no status
+  if (!workspace || workspace_bytes < sizeof(int32_t)) {
+    set_error("null workspace");
+    return TR_ERR_INVALID;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t word = 0;
+  cudaError_t e = cudaMemcpyAsync(&word, workspace, sizeof(word), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && reset && word != 0) e = cudaMemsetAsync(workspace, 0, sizeof(word), st);
+  if (e != cudaSuccess) {
+    set_error("reading the workspace status word: %s", cudaGetErrorString(e));
+    return TR_ERR_CUDA;
+  }
+  *status = word;
+  return TR_OK;
+}
+
+int tr_plan_set_wait_limit(tr_plan* plan, uint32_t polls) {
+  if (!plan) {
+    set_error("null plan");
+    return TR_ERR_INVALID;
+  }
+  plan->wait_limit = polls;
+  return TR_OK;
+}
+
 int tr_plan_tiling(const tr_plan* plan, int64_t tokens, tr_tiling* out) {
   if (!out) {
     set_error("null argument");
@@ -935,20 +858,13 @@ int tr_plan_tiling(const tr_plan* plan, int64_t tokens, tr_tiling* out) {
   MmaGeom g;
   DecodeGeom dg;
   TcGeom tg;
-  TcsGeom sg;
-  const int st = geom_for(plan, tokens, nullptr, &kind, &g, &dg, &tg, &sg);
+  const int st = geom_for(plan, tokens, nullptr, &kind, &g, &dg, &tg);
   if (st != TR_OK) return st;
   out->kernel = kind;
   if (kind == KIND_TC05) {
     out->tokens_per_tile = tg.TT;
     out->cluster = tg.CL;
     out->clusters = tg.NC;
-    return TR_OK;
-  }
-  if (kind == KIND_TCS) {
-    out->tokens_per_tile = (int32_t)tokens;
-    out->cluster = sg.CL;
-    out->clusters = sg.NC;
     return TR_OK;
   }
   if (kind == KIND_DECODE) {
@@ -970,8 +886,7 @@ static int forward_impl(const tr_plan* plan, const void* packed, const void* x, 
   MmaGeom g;
   DecodeGeom dg;
   TcGeom tg;
-  TcsGeom sg;
-  int st = geom_for(plan, tokens, tiling, &kind, &g, &dg, &tg, &sg);
+  int st = geom_for(plan, tokens, tiling, &kind, &g, &dg, &tg);
   if (st != TR_OK) return st;
   if (tokens == 0) return TR_OK;
   if (!packed || !x || !y) {
@@ -984,18 +899,6 @@ static int forward_impl(const tr_plan* plan, const void* packed, const void* x, 
   }
   if (kind == KIND_GENERIC) return launch_generic(*plan, packed, x, tokens, y, stream, epi);
   if (kind == KIND_DECODE) return launch_decode(*plan, dg, packed, x, tokens, y, stream, epi);
-  if (kind == KIND_TCS) {
-    if (!workspace || workspace_bytes < sg.ws_bytes) {
-      set_error("workspace of %zu bytes needed, %zu given", sg.ws_bytes,
-                workspace ? workspace_bytes : (size_t)0);
-      return TR_ERR_WORKSPACE;
-    }
-    if ((uintptr_t)workspace & 15) {
-      set_error("workspace must be 16-byte aligned");
-      return TR_ERR_ALIGN;
-    }
-    return launch_tcs(*plan, sg, packed, x, tokens, y, workspace, stream, epi);
-  }
   if (kind == KIND_TC05) {
     if (!workspace || workspace_bytes < tg.ws_bytes) {
       set_error("workspace of %zu bytes needed, %zu given", tg.ws_bytes,

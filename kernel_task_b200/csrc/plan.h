@@ -82,8 +82,7 @@ enum KernelKind {
   KIND_GENERIC = 1,
   KIND_MMA = 2,
   KIND_TC05 = 3,
-  KIND_DECODE = 4,
-  KIND_TCS = 5
+  KIND_DECODE = 4
 };
 
 struct Plan {
@@ -104,6 +103,9 @@ struct Plan {
   // every CTA needs a whole SM (the case of every kernel here).  Cluster placement is limited
   // per GPC, so this is below num_sms / c: 7 clusters of 16 CTAs on a 148-SM B200.
   int max_clusters[17];
+  // Polls of one bounded device-side wait before it gives up (0: the built-in limit, about a
+  // second of spinning).  Set by tr_plan_set_wait_limit; tests shorten it to make waits expire.
+  unsigned wait_limit;
 };
 
 // Fills out[c] (c = 1..16) for `device` by the CUDA occupancy query (cached per process);
@@ -161,21 +163,6 @@ struct TcGeom {
   size_t ws_bytes;
 };
 
-// Geometry of one launch of the small-T tcgen05 kernel (ring_tcs.cu): NGS sets of NGC o2 groups
-// (O2G modes each), the pieces of each set split over NC clusters of CL CTAs.
-struct TcsGeom {
-  int O2G, NG, NGC, NGS, CL, NC;
-  int MT1;             // 128-row tiles of S1 (rows (o1, u))
-  int N1C, N2C;        // MMA N of S1 (t, i2) and S2 (t, o1), padded to 16
-  int NB, NQ;          // G1/G3 ring slots; x slices staged
-  int d1_col, d2_col, d3_col, tmem_cols;
-  size_t off_a2, off_b1, off_a1, off_b3, off_b2, off_a3, off_ys, off_recv, off_bar;
-  size_t a2_stride, b1_bytes, a1_stride, b3_stride, b2_bytes, a3_stride;
-  int slot_elems;      // floats of one cluster's workspace slot (NC > 1)
-  size_t smem;
-  size_t ws_bytes;
-};
-
 // What a kernel writes for output element y[i] = v (v: the fp32 sum of the ring pieces):
 //   kind 0: v;  kind 1: aux[i] + v (residual add);  kind 2: silu(aux[i]) * v (gated MLP);
 // stored as fp32 when out_f32, else in the plan's element type.  aux is [T, d_out] row-major,
@@ -203,9 +190,6 @@ int forward_noalloc(const Plan& p, const void* packed, const void* x, int64_t T,
                     void* stream);
 int resolve_decode_geom(const Plan& p, int64_t T, const tr_tiling* force, DecodeGeom* g);
 int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* force, TcGeom* g);
-int resolve_tcs_geom(const Plan& p, int64_t T, const tr_tiling* force, TcsGeom* g);
-int launch_tcs(const Plan& p, const TcsGeom& g, const void* packed, const void* x, int64_t T,
-               void* y, void* ws, void* stream, const Epi& epi);
 int launch_tc05(const Plan& p, const TcGeom& g, const void* packed, const void* x, int64_t T,
                 void* y, void* ws, void* stream, const Epi& epi);
 int decode_variant(const Plan& p);

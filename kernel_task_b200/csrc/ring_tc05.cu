@@ -39,9 +39,11 @@
 //       lanes of a store phase hit eight different bank groups
 //   A1, B1, B2, A3, B3  no swizzle: 8 rows x 16 B core matrices, LBO 128 B, SBO = K/8 * 128 B
 //
-// Every wait on an mbarrier is bounded; on expiry the CTA raises a shared abort flag (all later
-// waits return at once), records TR_ERR_TIMEOUT in the status word, waits (bounded) for its own
-// bulk copies and tensor-core work in flight, releases its TMEM and returns.
+// Every wait on an mbarrier is bounded (TcParams::spin_limit polls); on expiry the CTA raises a
+// shared abort flag (all later waits return at once), records TR_ERR_TIMEOUT in the status word
+// (the first workspace word, read by tr_workspace_status), waits (bounded) for its own bulk
+// copies in flight, and returns.  The two issuing warps always wait for their own tensor-core
+// work before the CTA barrier that precedes the TMEM release.
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
@@ -74,7 +76,7 @@ enum {
   BAR_B3FULL = 32,  // [16] B3 landed (slot 0 only when the whole range loads at once)
   BAR_B2FULL = 48,  // B2 landed
   BAR_D3DONE = 49,  // commit after the last S3: every tensor-core operation completed
-  BAR_DRAIN = 50,   // [2] after a timeout: the two issuing warps' own work completed
+  BAR_DRAIN = 50,   // [2] after the piece loop: the two issuing warps' own work completed
   BAR_C1DONE = 52,  // [2] C1 warps finished piece j (count 8), index j % 2
   BAR_C2DONE = 54,  // [2] C2 warps finished piece j (count 4), index j % 2
   BAR_D1READ = 56,  // [2] C1 warps read D1(j) (count 8), index j % 2
@@ -100,6 +102,7 @@ struct TcParams {
   int ystr, vec_out, slot_elems;
   float* parts;    // per-CTA partial sums in the workspace (CL > 1)
   int part_elems;  // floats of one CTA's partial sums
+  unsigned spin_limit;  // polls of one bounded wait before it gives up (tr_plan_set_wait_limit)
   Epi epi;  // what is written for each y element
 };
 
@@ -244,12 +247,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
     const int q = (pa + k) / sh.R - i3a;
     bool ok = true;
     if (q != s1_q_seen) {
-      ok = warp_wait(bar(BAR_A1FULL + (q & 1)), (q >> 1) & 1, abort);
+      ok = warp_wait(bar(BAR_A1FULL + (q & 1)), (q >> 1) & 1, abort, p.spin_limit);
       s1_q_seen = q;
     }
     if (ok && !s1_b1_seen) {
-      ok = p.b1_all ? warp_wait(bar(BAR_G1FULL), 0, abort)
-                    : warp_wait(bar(BAR_G1FULL + k % NB1), (k / NB1) & 1, abort);
+      ok = p.b1_all ? warp_wait(bar(BAR_G1FULL), 0, abort, p.spin_limit)
+                    : warp_wait(bar(BAR_G1FULL + k % NB1), (k / NB1) & 1, abort, p.spin_limit);
       s1_b1_seen = p.b1_all;
     }
     if (!ok) return false;
@@ -286,14 +289,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
       // issued after a timeout only computes values the caller discards.
       // ---- S1(j + ND1) into the D1 buffer C1 has just read (separate arrangement)
       if (ok && !p.shared_d12 && j + p.ND1 < np) {
-        ok = warp_wait(bar(BAR_D1READ + (j & 1)), (j >> 1) & 1, abort);
+        ok = warp_wait(bar(BAR_D1READ + (j & 1)), (j >> 1) & 1, abort, p.spin_limit);
         if (ok) ok = issue_s1(j + p.ND1);
       }
       // ---- S2(j): C1(j) wrote A2(j); the D2 buffer's previous piece was read by C2
-      if (ok) ok = warp_wait(bar(BAR_C1DONE + (j & 1)), (j >> 1) & 1, abort);
-      if (ok && !b2ok) ok = b2ok = warp_wait(bar(BAR_B2FULL), 0, abort);
+      if (ok) ok = warp_wait(bar(BAR_C1DONE + (j & 1)), (j >> 1) & 1, abort, p.spin_limit);
+      if (ok && !b2ok) ok = b2ok = warp_wait(bar(BAR_B2FULL), 0, abort, p.spin_limit);
       if (ok && !p.shared_d12 && j >= 2)
-        ok = warp_wait(bar(BAR_D2READ + (j & 1)), ((j >> 1) - 1) & 1, abort);
+        ok = warp_wait(bar(BAR_D2READ + (j & 1)), ((j >> 1) - 1) & 1, abort, p.spin_limit);
       if (ok) {
         const uint32_t a2 = a2s + (j % p.NA2) * p.a2_bytes;
         for (int ks = 0; ks < sh.KS2; ++ks)
@@ -302,10 +305,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
         commit_one(bar(BAR_S2DONE + (j & 1)));
       }
     }
-    if (*abort) {  // drain this warp's tensor-core work
-      commit_one(bar(BAR_DRAIN));
-      if (lane == 0) mbar_drain(bar(BAR_DRAIN), 0);
-    }
+    // Drain this warp's tensor-core work before the CTA barrier that precedes the TMEM release,
+    // whatever happened: another warp may raise the abort flag after this loop issued its last
+    // MMA, and then no one waits for D3DONE.
+    commit_one(bar(BAR_DRAIN));
+    if (lane == 0) mbar_drain_spin(bar(BAR_DRAIN), 0);
     __syncwarp();
   } else if (warp == 13) {
     // ===================== issuer B: S3 of each piece (and S1, shared buffers) ================
@@ -316,14 +320,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
     for (int j = 0; j < np; ++j) {
       // ---- S1(j + 2) into the buffer whose D2(j) C2 has just read (shared arrangement)
       if (ok && p.shared_d12 && j + 2 < np) {
-        ok = warp_wait(bar(BAR_D2READ + (j & 1)), (j >> 1) & 1, abort);
+        ok = warp_wait(bar(BAR_D2READ + (j & 1)), (j >> 1) & 1, abort, p.spin_limit);
         if (ok) ok = issue_s1(j + 2);
       }
       // ---- S3(j): C2(j) wrote A3(j); B3 landed
-      if (ok) ok = warp_wait(bar(BAR_C2DONE + (j & 1)), (j >> 1) & 1, abort);
+      if (ok) ok = warp_wait(bar(BAR_C2DONE + (j & 1)), (j >> 1) & 1, abort, p.spin_limit);
       if (ok)
-        ok = p.b3_all ? warp_wait(bar(BAR_B3FULL), 0, abort)
-                      : warp_wait(bar(BAR_B3FULL + j % p.NB3), (j / p.NB3) & 1, abort);
+        ok = p.b3_all ? warp_wait(bar(BAR_B3FULL), 0, abort, p.spin_limit)
+                      : warp_wait(bar(BAR_B3FULL + j % p.NB3), (j / p.NB3) & 1, abort, p.spin_limit);
       if (ok) {
         const uint32_t a3 = a3s + (j % p.NA3) * p.a3_bytes;
         const uint32_t b3 = b3s + (p.b3_all ? j : j % p.NB3) * p.b3_bytes;
@@ -334,10 +338,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
         if (j == np - 1) commit_one(bar(BAR_D3DONE));
       }
     }
-    if (*abort) {  // drain this warp's tensor-core work
-      commit_one(bar(BAR_DRAIN + 1));
-      if (lane == 0) mbar_drain(bar(BAR_DRAIN + 1), 0);
-    }
+    commit_one(bar(BAR_DRAIN + 1));  // drain this warp's tensor-core work (as issuer A)
+    if (lane == 0) mbar_drain_spin(bar(BAR_DRAIN + 1), 0);
     __syncwarp();
   } else {
     // ---- first x slices, staged by the converter and feeder warps
@@ -379,9 +381,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
       bool ok = true;
       for (int j = 0; j < np; ++j) {
         const int ab = j % p.NA2;
-        if (ok) ok = mbar_spin(bar(BAR_S1DONE + (j & 3)), (j >> 2) & 1, abort);
+        if (ok) ok = mbar_spin(bar(BAR_S1DONE + (j & 3)), (j >> 2) & 1, abort, p.spin_limit);
         if (ok && j >= p.NA2)  // S2 of the piece that last used this A2 buffer completed
-          ok = mbar_spin(bar(BAR_S2DONE + ((j - p.NA2) & 1)), ((j - p.NA2) >> 1) & 1, abort);
+          ok = mbar_spin(bar(BAR_S2DONE + ((j - p.NA2) & 1)), ((j - p.NA2) >> 1) & 1, abort, p.spin_limit);
         bool d1_read = false;
         if (ok) {
           unsigned char* a2 = smem + p.off_a2 + ab * p.a2_bytes;
@@ -440,9 +442,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
       bool ok = true;
       for (int j = 0; j < np; ++j) {
         const int db = j & 1, ab = j % p.NA3;
-        if (ok) ok = mbar_spin(bar(BAR_S2DONE + db), (j >> 1) & 1, abort);
+        if (ok) ok = mbar_spin(bar(BAR_S2DONE + db), (j >> 1) & 1, abort, p.spin_limit);
         if (ok && j >= p.NA3)  // S3 of the piece that last used this A3 buffer completed
-          ok = mbar_spin(bar(BAR_S3DONE + ((j - p.NA3) & 15)), ((j - p.NA3) >> 4) & 1, abort);
+          ok = mbar_spin(bar(BAR_S3DONE + ((j - p.NA3) & 15)), ((j - p.NA3) >> 4) & 1, abort, p.spin_limit);
         if (ok) {
           const uint32_t d2 = tmem + lane_base + d2_col(j);
           unsigned char* rowp =
@@ -526,7 +528,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
           __nanosleep(64);
         }
       }
-      if (lane == 0 && np > 0 && *abort) {  // drain this CTA's bulk copies before leaving
+      // wait for this CTA's bulk copies before the operand space is reused, also when the loop
+      // ended normally and another warp raised the abort flag later (normally each was already
+      // consumed, so every test succeeds at once)
+      if (lane == 0 && np > 0) {
         mbar_drain(bar(BAR_B2FULL), 0);
         if (p.b1_all) mbar_drain(bar(BAR_G1FULL), 0);
         else
@@ -548,7 +553,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   float* ys = reinterpret_cast<float*>(smem);
   const int ystr = p.ystr;
   if (warp < 12) {
-    const bool ok = np > 0 && mbar_spin(bar(BAR_D3DONE), 0, abort);
+    const bool ok = np > 0 && mbar_spin(bar(BAR_D3DONE), 0, abort, p.spin_limit);
     tc_fence_after();
     const int r = 32 * (warp & 3) + lane;
     const bool vec4 = (sh.O3 & 3) == 0;
@@ -820,6 +825,7 @@ static void fill_tc(TcParams<S>& tp, const Plan& p, const TcGeom& g, const void*
   tp.vec_out = c.sy3 == 1 && c.O3 % 8 == 0 && c.sy1 % 8 == 0 && c.sy2 % 8 == 0 &&
                c.d_out % 8 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
   tp.slot_elems = 128 * t.O2G * p.c.O3;
+  tp.spin_limit = p.wait_limit ? p.wait_limit : kSpinLimit;
 }
 
 template <class S, typename E>

@@ -1,4 +1,4 @@
-// Shared helpers of the tcgen05 kernels (ring_tc05.cu, ring_tcs.cu): UMMA shared-memory
+// Shared helpers of the tcgen05 kernels (ring_tc05.cu): UMMA shared-memory
 // descriptors and instruction descriptors, single-lane MMA issue and commit, tcgen05 fences,
 // bounded mbarrier waits, TMA bulk copies, named barriers and TMEM loads.
 #pragma once
@@ -105,10 +105,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, volati
 
 
 // Spinning bounded wait of one thread (test_wait polls; the abort flag is checked every 256).
-__device__ __forceinline__ bool mbar_spin(uint32_t mbar, uint32_t parity, volatile int* abort) {
+// `limit` polls without completion make the wait give up and raise the CTA's abort flag.
+__device__ __forceinline__ bool mbar_spin(uint32_t mbar, uint32_t parity, volatile int* abort,
+                                          unsigned limit = kSpinLimit) {
   for (unsigned i = 0; !mbar_test(mbar, parity); ++i) {
     if ((i & 255) == 255 && *abort) return false;
-    if (i >= kSpinLimit) {
+    if (i >= limit) {
       *abort = 1;
       return false;
     }
@@ -120,14 +122,23 @@ __device__ __forceinline__ bool mbar_spin(uint32_t mbar, uint32_t parity, volati
 // the suspending try_wait: the MMA-issuing warps sit on the critical path of every ring piece,
 // and a suspended warp resumed 0.1-0.25 us after the phase completed (measured with globaltimer
 // marks; spinning cut the c2 T = 32 call from 57 to 50 us).
-__device__ __forceinline__ bool warp_wait(uint32_t mbar, uint32_t parity, volatile int* abort) {
-  return __all_sync(0xffffffffu, mbar_spin(mbar, parity, abort));
+__device__ __forceinline__ bool warp_wait(uint32_t mbar, uint32_t parity, volatile int* abort,
+                                          unsigned limit = kSpinLimit) {
+  return __all_sync(0xffffffffu, mbar_spin(mbar, parity, abort, limit));
 }
 
 // Bounded wait that ignores the abort flag: draining the CTA's own work in flight.
 __device__ __forceinline__ void mbar_drain(uint32_t mbar, uint32_t parity) {
   if (mbar_test(mbar, parity)) return;
   for (unsigned i = 0; i < kWaitLimit && !mbar_try(mbar, parity); ++i) {
+  }
+}
+
+// Spinning bounded wait that ignores the abort flag: an issuing warp waits for its own
+// tensor-core work on every exit path (it completes on its own, so the bound is never reached
+// in practice).
+__device__ __forceinline__ void mbar_drain_spin(uint32_t mbar, uint32_t parity) {
+  for (unsigned i = 0; i < kSpinLimit && !mbar_test(mbar, parity); ++i) {
   }
 }
 

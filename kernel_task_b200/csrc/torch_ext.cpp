@@ -9,6 +9,7 @@
 #include <pybind11/pybind11.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
 #include <memory>
 #include <string>
 #include <vector>
@@ -47,6 +48,10 @@ class RingOp {
       s.output_modes[k] = (int32_t)out_modes[k];
     }
     s.rank = (int32_t)rank;
+    // TRR_CHECK_STATUS=1: after every call, read the workspace status word (a stream
+    // synchronisation) and raise if a bounded device-side wait gave up.  Debugging aid.
+    const char* chk = std::getenv("TRR_CHECK_STATUS");
+    check_status_ = chk && chk[0] == '1';
     const int code = dtype_code(dtype);
     if (code < 0) throw py::value_error("cores must be float32, float16 or bfloat16");
     tr_plan* p = nullptr;
@@ -124,6 +129,7 @@ class RingOp {
       st = tr_forward_tiled(plan_.get(), packed_.data_ptr(), x.data_ptr(), T, y.data_ptr(),
                             ws_bytes_ ? ws_.data_ptr() : nullptr, ws_bytes_, tiling, stream);
       if (st != TR_OK) raise_status(st, "tr_forward");
+      if (check_status_) check_device_status();
       return y;
     }
     tr_epilogue e;
@@ -134,7 +140,34 @@ class RingOp {
     st = tr_forward_epilogue(plan_.get(), packed_.data_ptr(), x.data_ptr(), T, y.data_ptr(), &e,
                              ws_bytes_ ? ws_.data_ptr() : nullptr, ws_bytes_, tiling, stream);
     if (st != TR_OK) raise_status(st, "tr_forward_epilogue");
+    if (check_status_) check_device_status();
     return y;
+  }
+
+  // The workspace's device status word (TR_OK, or TR_ERR_TIMEOUT after a bounded wait gave
+  // up); synchronises the current stream; `reset` clears the word.
+  int64_t workspace_status(bool reset) {
+    int32_t status = TR_OK;
+    if (ws_bytes_ == 0) return TR_OK;
+    c10::cuda::CUDAGuard guard((c10::DeviceIndex)device_);
+    const int st = tr_workspace_status(
+        ws_.data_ptr(), ws_bytes_, &status, reset ? 1 : 0,
+        at::cuda::getCurrentCUDAStream((c10::DeviceIndex)device_).stream());
+    if (st != TR_OK) raise_status(st, "tr_workspace_status");
+    return status;
+  }
+
+  void check_device_status() {
+    const int64_t status = workspace_status(true);
+    if (status != TR_OK)
+      throw std::runtime_error(std::string("tensor-ring kernel: ") +
+                               tr_status_string((int)status) + " (the call's output is not valid)");
+  }
+
+  // Polls of a bounded device-side wait before it gives up (0 = built-in limit).
+  void set_wait_limit(int64_t polls) {
+    const int st = tr_plan_set_wait_limit(plan_.get(), (uint32_t)polls);
+    if (st != TR_OK) raise_status(st, "tr_plan_set_wait_limit");
   }
 
   at::Tensor call(const at::Tensor& x) { return forward_impl(x, nullptr); }
@@ -222,6 +255,7 @@ class RingOp {
   at::Tensor packed_;
   at::Tensor ws_;
   size_t ws_bytes_ = 0;
+  bool check_status_ = false;
 };
 
 void check_consume_f32(const at::Tensor& t, const at::Tensor& like, const char* what) {
@@ -287,6 +321,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("describe", &RingOp::describe)
       .def("flops_per_token", &RingOp::flops_per_token)
       .def("workspace_bytes", &RingOp::workspace_bytes)
+      .def("workspace_status", &RingOp::workspace_status, py::arg("reset") = true)
+      .def("set_wait_limit", &RingOp::set_wait_limit, py::arg("polls"))
       .def_property_readonly("packed", &RingOp::packed)
       .def_property_readonly("workspace", &RingOp::workspace);
   m.def("empty_launch", &empty_launch, "launch an empty kernel on the current stream");

@@ -284,3 +284,19 @@ def test_epilogue_and_consumer_arguments_need_no_device():
 
 def lib_call(name, *args):
     return getattr(abi.lib(), name)(*args)
+
+
+def test_workspace_status_and_wait_limit_arguments_need_no_device():
+    """tr_workspace_status / tr_plan_set_wait_limit: argument errors before any CUDA call; a
+    zero-byte workspace (decode and mma kernels) has no status word and reads TR_OK."""
+    L = abi.lib()
+    st = ctypes.c_int32(123)
+    assert L.tr_workspace_status(None, 0, ctypes.byref(st), 1, None) == abi.TR_OK
+    assert st.value == abi.TR_OK
+    assert L.tr_workspace_status(None, 0, None, 1, None) == abi.TR_ERR_INVALID
+    assert L.tr_workspace_status(None, 256, ctypes.byref(st), 1, None) == abi.TR_ERR_INVALID
+    assert L.tr_plan_set_wait_limit(None, 1) == abi.TR_ERR_INVALID
+    s = kspec.SPEC_C1
+    p = abi.Plan(s.input_modes, s.output_modes, s.rank, abi.TR_F16)
+    p.set_wait_limit(1)
+    p.set_wait_limit(0)

@@ -64,7 +64,7 @@ KERNEL_NAMES = {1: "ring_generic_kernel", 2: "ring_mma_kernel", 3: "ring_tc05_ke
 # the reference install (baseline/build_reference.py); absent -> those legs report why
 REF_SITE = ROOT / "baseline" / "_ref" / "site"
 REF_EXT = ROOT / "baseline" / "_ref" / "tree" / "build" / "tr_ring_ext" / "tr_ring_ext.so"
-# the V3 tilings of the reference's published T=1 runs, forced (BASELINE: H100_TUNED values)
+# the V3 tilings of the reference's published T=1 runs (its H100_TUNED values), forced
 REF_FORCED = {8: {"TR_KC": "2", "TR_QC": "4", "TR_TT": "1"},
               16: {"TR_KC": "4", "TR_QC": "4", "TR_TT": "1"}}
 
@@ -571,7 +571,7 @@ def prefill_leg(args, rank, world, dev, tc_peak, tc_sustained):
 
 
 def c3_leg(dev, flush, tokens, tc_peak, dense=True):
-    """Config 3: 4096 -> 14336, modes (16,16,16)->(16,28,32), R32, bf16 (seeded BASELINE
+    """Config 3: 4096 -> 14336, modes (16,16,16)->(16,28,32), R32, bf16 (seeded benchmark
     inputs): cold device time per call (L2 flushed), our kernel and the dense bars."""
     from kernel_task_b200 import prepare_optimized
     from kernel_task_b200.spec import SPEC_C3, baseline_cores, baseline_x

@@ -20,7 +20,7 @@ LIB = PKG / "libtrring.so"
 EXT = PKG / "_trring_torch.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_SOURCES = ["plan.cpp", "pack.cu", "ring_generic.cu", "ring_mma.cu", "ring_decode.cu",
-                "ring_tc05.cu", "consume.cu"]
+                "ring_tc05.cu", "ring_slab.cu", "consume.cu"]
 
 
 def _nvcc() -> str:

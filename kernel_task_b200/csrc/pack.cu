@@ -1,6 +1,7 @@
 // Preparation: pack the caller's three cores [R, o, i, R] into kernel-native layouts.
 //
-// Replaces pack_cores (factorized_inference/tr_kernel.py:86-99).  Two layouts exist:
+// Replaces pack_cores (factorized_inference/tr_kernel.py:86-99).  The layouts (plan.h describes
+// the tcgen05 and slab operand layouts):
 //   * generic  -- the canonical cores G1, G2, G3 in natural [l][o][i][r] order, plan dtype;
 //   * mma      -- m16n8k16 B-operand fragments (one uint2 per lane per (k-step, n-tile)):
 //                   G1 frags  [s][ks1][nt1][lane]       K = i1,     N = (o1,u)   plan dtype
@@ -179,6 +180,60 @@ __global__ void pack_tc_kernel(CoreView<E> c0, CoreView<E> c1, CoreView<E> c2, T
   }
 }
 
+struct SlabPackDims {
+  int I1, I2, I3, O1, O2, O3, R, K1P, NSL, RV, N1S, KSL, K2S, O2G, N2, N3P, K3P, npieces;
+};
+
+// Slab-kernel operands (ring_slab.cu): B1 per (s, sl) [N1S rows (o1, ul)] x [K1P i1] in the input
+// dtype E, with u = 8 sl + ul; B2 per o2 group [N2 rows (o2, v)] x [K2S (sl, i2, ul)] and B3 per
+// piece [N3P rows o3] x [K3P v] in fp16; zero where a padded index has no core entry.
+template <typename E>
+__global__ void pack_slab_kernel(CoreView<E> c0, CoreView<E> c1, CoreView<E> c2, SlabPackDims d,
+                                 unsigned char* b1, unsigned char* b2, unsigned char* b3,
+                                 size_t n1, size_t n2, size_t n3) {
+  const size_t total = n1 + n2 + n3;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    if (idx < n1) {
+      const int k = (int)(idx % d.K1P);
+      size_t q = idx / d.K1P;
+      const int n = (int)(q % d.N1S);
+      q /= d.N1S;
+      const int sl = (int)(q % d.NSL);
+      const int s = (int)(q / d.NSL);
+      const int o1 = n / 8, u = 8 * sl + n % 8;
+      const float v = (o1 < d.O1 && u < d.R && k < d.I1) ? c0.at(s, o1, k, u) : 0.f;
+      *reinterpret_cast<E*>(b1 + ((size_t)s * d.NSL + sl) * d.N1S * d.K1P * sizeof(E) +
+                            umma_kmajor_offset(n, k, d.K1P)) = from_f32<E>(v);
+      continue;
+    }
+    float v;
+    unsigned char* dst;
+    if (idx < n1 + n2) {
+      const size_t e = idx - n1;
+      const int k = (int)(e % d.K2S);
+      size_t q = e / d.K2S;
+      const int n = (int)(q % d.N2);
+      const int grp = (int)(q / d.N2);
+      const int o2 = grp * d.O2G + n / d.RV, vv = n % d.RV;
+      const int sl = k / d.KSL, kk = k % d.KSL;
+      const int i2 = kk / 8, u = 8 * sl + kk % 8;
+      v = (o2 < d.O2 && vv < d.R && i2 < d.I2 && u < d.R) ? c1.at(u, o2, i2, vv) : 0.f;
+      dst = b2 + (size_t)grp * d.N2 * d.K2S * 2 + umma_kmajor_offset(n, k, d.K2S);
+    } else {
+      const size_t e = idx - n1 - n2;
+      const int k = (int)(e % d.K3P);
+      size_t q = e / d.K3P;
+      const int n = (int)(q % d.N3P);
+      const int piece = (int)(q / d.N3P);
+      const int i3 = piece / d.R, s = piece % d.R;
+      v = (n < d.O3 && k < d.R) ? c2.at(k, n, i3, s) : 0.f;
+      dst = b3 + (size_t)piece * d.N3P * d.K3P * 2 + umma_kmajor_offset(n, k, d.K3P);
+    }
+    *reinterpret_cast<__half*>(dst) = __float2half_rn(v);
+  }
+}
+
 template <typename E>
 static int pack_typed(const Plan& p, const void* const cores[3], void* packed, cudaStream_t st) {
   const Canon& c = p.c;
@@ -218,6 +273,19 @@ static int pack_typed(const Plan& p, const void* const cores[3], void* packed, c
             v[0], v[1], v[2], td, reinterpret_cast<unsigned char*>(base + t.off_b1),
             reinterpret_cast<unsigned char*>(base + t.off_b2),
             reinterpret_cast<unsigned char*>(base + t.off_b3), tn1, tn2, tn3);
+      }
+      if (p.slab_ok) {
+        const SlabLayout& l = p.sl;
+        SlabPackDims sd{c.I1, c.I2, c.I3, c.O1, c.O2, c.O3, c.R, m.K1P, l.NSL, l.RV, l.N1S,
+                        l.KSL, l.K2S, l.O2G, l.N2, l.N3P, l.K3P, m.npieces};
+        const size_t sn1 = (size_t)c.R * l.NSL * l.N1S * m.K1P;
+        const size_t sn2 = (size_t)l.NG * l.N2 * l.K2S;
+        const size_t sn3 = (size_t)m.npieces * l.N3P * l.K3P;
+        const int sb = (int)std::min<size_t>((sn1 + sn2 + sn3 + 255) / 256, 4096);
+        pack_slab_kernel<E><<<sb, 256, 0, st>>>(
+            v[0], v[1], v[2], sd, reinterpret_cast<unsigned char*>(base + l.off_b1),
+            reinterpret_cast<unsigned char*>(base + l.off_b2),
+            reinterpret_cast<unsigned char*>(base + l.off_b3), sn1, sn2, sn3);
       }
     }
   }

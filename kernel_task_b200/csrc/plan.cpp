@@ -206,6 +206,103 @@ static void build_tc_layout(Plan* p) {
   p->tc_ok = p->mma_ok && t.tmem_cols <= 512;
 }
 
+// Shared memory of one slab-kernel CTA (ring_slab.cu), relative to a 1024-byte aligned base:
+//   A2 slab slots x NA2 (128-byte swizzle, 64-wide K slabs of 128 rows), B2 of the group,
+//   A3 x NA3 (S3 A operands of the group's o2), A1 x 2 (x slices), B1 slab slices x NB1,
+//   B3 x NB3; reused after the piece loop as the CTA's fp32 partial y [128 rows x ystr];
+//   then the mbarriers.  `total` includes 1 KB of slack for aligning the window.
+struct SlabSmem {
+  size_t a2_bytes, a3_bytes, a1_bytes;
+  size_t off_a2, off_b2, off_a3, off_a1, off_g1, off_b3, off_bar, total;
+};
+
+static SlabSmem slab_smem(const Plan& p, const SlabLayout& l, int NA2, int NA3, int NB1,
+                          int NB3) {
+  const MmaLayout& m = p.m;
+  SlabSmem s;
+  s.a2_bytes = (size_t)ceil_div(l.KSL, 64) * 128 * 128;
+  s.a3_bytes = (size_t)l.O2G * 128 * l.K3P * 2;
+  s.a1_bytes = (size_t)128 * m.K1P * 2;
+  const size_t b1 = (size_t)l.N1S * m.K1P * elem_size(p.dtype);
+  const size_t b2 = (size_t)l.N2 * l.K2S * 2;
+  const size_t b3 = (size_t)l.N3P * l.K3P * 2;
+  s.off_a2 = 0;
+  s.off_b2 = (size_t)NA2 * s.a2_bytes;
+  s.off_a3 = align_up(s.off_b2 + b2, 128);
+  s.off_a1 = align_up(s.off_a3 + NA3 * s.a3_bytes, 128);
+  s.off_g1 = align_up(s.off_a1 + 2 * s.a1_bytes, 128);
+  s.off_b3 = align_up(s.off_g1 + NB1 * b1, 128);
+  const size_t main = s.off_b3 + NB3 * b3;
+  const size_t ys = (size_t)128 * tc_ystr(p, l.O2G) * 4;  // partial y overlays the operands
+  s.off_bar = align_up(std::max(main, ys), 128);
+  s.total = s.off_bar + 1024 + 1024;
+  return s;
+}
+
+// Slab-kernel operand layout (appended after the other packed layouts).  O2 is split into NG
+// groups so that a CTA's TMEM holds two D1 slab buffers, ND2 D2 buffers and the S3 accumulators
+// of its group within 512 columns, and its operands fit in shared memory; of the two D2 depths
+// the one giving fewer groups wins (less repeated S1 and C1 work), two buffers on a tie.
+// Needs ranks <= 32, O1 <= 32 (one D1 slab of at most 256 columns) and fp16/bf16.
+static void build_slab_layout(Plan* p) {
+  const Canon& c = p->c;
+  SlabLayout& l = p->sl;
+  p->slab_ok = 0;
+  if (p->dtype == TR_F32 || c.R > 32 || c.O1 > 32 || c.I2 > 128) return;
+  l.NSL = ceil_div(c.R, 8);
+  l.RV = 8 * l.NSL;
+  l.N1S = ceil_div(c.O1 * 8, 16) * 16;
+  l.KSL = ceil_div(c.I2 * 8, 16) * 16;
+  l.K2S = l.NSL * l.KSL;
+  l.N3P = ceil_div(c.O3, 16) * 16;
+  l.K3P = std::max(16, ceil_div(l.RV, 16) * 16);
+  if (l.N3P > 256) return;
+  // the last TMEM column a C1 warp reads (16-column loads from the start of its o1 half)
+  const int h = (c.O1 + 1) / 2;
+  const int c1_reach = l.N1S + std::max(ceil_div(h * 8, 16) * 16,
+                                        h * 8 + ceil_div((c.O1 - h) * 8, 16) * 16);
+  const int step = (l.RV % 16 == 0) ? 1 : 2;  // S2's N = O2G * RV must be a multiple of 16
+  auto tmem_need = [&](int nd2, int o2g) {
+    return std::max(2 * l.N1S + nd2 * o2g * l.RV + o2g * l.N3P, c1_reach);
+  };
+  auto fits = [&](int nd2, int o2g) {
+    SlabLayout t = l;
+    t.O2G = o2g;
+    t.N2 = o2g * l.RV;
+    t.ND2 = nd2;
+    return tmem_need(nd2, o2g) <= 512 && slab_smem(*p, t, 2, 1, 2, 4).total <= p->smem_optin;
+  };
+  int best_nd2 = 0, best_w = 0, best_ng = 0;
+  for (int nd2 = 2; nd2 >= 1; --nd2) {
+    int o2g = std::min(ceil_div(c.O2, step) * step, 256 / l.RV);
+    o2g -= o2g % step;
+    while (o2g >= step && !fits(nd2, o2g)) o2g -= step;
+    if (o2g < step) continue;
+    int w = ceil_div(c.O2, ceil_div(c.O2, o2g));  // balanced width, same group count
+    if (w % step) w += step - w % step;
+    w = std::min(w, o2g);
+    const int ng = ceil_div(c.O2, w);
+    if (best_nd2 == 0 || ng < best_ng) {
+      best_nd2 = nd2;
+      best_w = w;
+      best_ng = ng;
+    }
+  }
+  if (best_nd2 == 0) return;
+  l.ND2 = best_nd2;
+  l.O2G = best_w;
+  l.NG = best_ng;
+  l.N2 = l.O2G * l.RV;
+  l.d2_col = 2 * l.N1S;
+  l.d3_col = l.d2_col + l.ND2 * l.N2;
+  l.tmem_cols = 32;
+  while (l.tmem_cols < tmem_need(l.ND2, l.O2G)) l.tmem_cols *= 2;
+  l.bytes_b1 = (size_t)l.N1S * p->m.K1P * elem_size(p->dtype);
+  l.bytes_b2 = (size_t)l.N2 * l.K2S * 2;
+  l.bytes_b3 = (size_t)l.N3P * l.K3P * 2;
+  p->slab_ok = l.tmem_cols <= 512;
+}
+
 static void build_generic_layout(Plan* p) {
   const Canon& c = p->c;
   GenericLayout& g = p->g;
@@ -419,7 +516,13 @@ int resolve_decode_geom(const Plan& p, int64_t T, const tr_tiling* f, DecodeGeom
     set_error("decode kernel: %lld tokens x %d S1 rows exceed two m16 tiles", (long long)T, c.I2);
     return TR_ERR_UNSUPPORTED;
   }
-  const int CL = (f && f->cluster > 0) ? f->cluster : std::min(16, m.npieces);
+  int CL = (f && f->cluster > 0) ? f->cluster : std::min(16, m.npieces);
+  if (!(f && f->cluster > 0)) {
+    // one wave: smaller clusters when the fewest o2 chunks the compiled kernel allows do not
+    // all fit on the device at once (2880 -> 1920 at R8: 8 chunks, but only 7 clusters of 16)
+    const int noc_min = ceil_div(c.O2, decode_max_o2c(variant, g->MT2));
+    while (CL > 1 && noc_min > p.max_clusters[CL]) CL = (CL + 1) / 2;
+  }
   if (CL < 1 || CL > 16 || CL > m.npieces) {
     set_error("cluster=%d invalid for %d pieces", CL, m.npieces);
     return TR_ERR_INVALID;
@@ -559,6 +662,134 @@ int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* f, TcGeom* g) {
   return TR_OK;
 }
 
+// Split of the slab kernel's pieces for `cols` tile columns, as tc_split: among the splits whose
+// cols * NC clusters of CL CTAs are co-resident (one wave), the least estimated time: the
+// longest CTA's pieces at about 0.3 us per rank slab, 1 us per extra x slice, and with NC > 1
+// the slot pass (2 us plus the slot traffic, NC / CL of a tile's partial sums at 1.4 us per
+// 69 KB).  With a column per SM or more, one CTA per column.
+static void slab_split(const Plan& p, long long cols, int64_t rows, int* CL, int* NC) {
+  const Canon& c = p.c;
+  const MmaLayout& m = p.m;
+  const SlabLayout& l = p.sl;
+  *CL = 1;
+  *NC = 1;
+  if (cols >= p.num_sms) return;
+  const double piece_us = 0.3 * l.NSL;
+  const double part_kb = (double)rows * l.O2G * c.O3 * 4 / 1024.0;
+  double best = 1e30;
+  for (int cl = 16; cl >= 1; cl /= 2) {
+    if (cl > m.npieces || cols > p.max_clusters[cl]) continue;
+    const long long nc_max =
+        std::min<long long>(std::min<long long>(p.max_clusters[cl] / cols, m.npieces / cl), 5);
+    for (int nc = 1; nc <= nc_max; ++nc) {
+      const int NJ = cl * nc;
+      double est = piece_us * ceil_div(m.npieces, NJ) +
+                   1.0 * (max_i3_span(m.npieces, c.R, NJ) - 1);
+      if (nc > 1) est += 2.0 + 1.4 * ((double)nc / cl) * part_kb / 67.5;
+      if (est < best - 1e-9) {
+        best = est;
+        *CL = cl;
+        *NC = nc;
+      }
+    }
+  }
+}
+
+// Slab geometry: row tiles of TT tokens (TT*O1 and TT*I2 <= 128), NG o2 groups, NJ = CL*NC CTAs
+// over the pieces of each (tile, group); the deepest operand rings that fit.
+int resolve_slab_geom(const Plan& p, int64_t T, const tr_tiling* f, SlabGeom* g) {
+  const Canon& c = p.c;
+  const MmaLayout& m = p.m;
+  const SlabLayout& l = p.sl;
+  if (!p.slab_ok) {
+    set_error("slab kernel does not support this spec/dtype");
+    return TR_ERR_UNSUPPORTED;
+  }
+  const int tt_max = std::max(1, std::min(128 / c.O1, 128 / c.I2));
+  int TT = (f && f->tokens_per_tile > 0) ? f->tokens_per_tile : tt_max;
+  if (TT > T) TT = (int)T;
+  if (TT < 1) TT = 1;
+  if (TT > tt_max) {
+    set_error("tokens_per_tile=%d exceeds the 128-row tile (at most %d tokens: O1=%d, I2=%d)",
+              TT, tt_max, c.O1, c.I2);
+    return TR_ERR_INVALID;
+  }
+  g->TT = TT;
+  g->ntiles = (int)((T + TT - 1) / TT);
+  int CL, NC;
+  if (f && f->cluster > 0) {
+    CL = f->cluster;
+    NC = f->clusters > 0 ? f->clusters : 1;
+  } else {
+    const long long cols = std::max<long long>(1, (long long)g->ntiles * l.NG);
+    slab_split(p, cols, std::min<int64_t>(T, TT) * c.O1, &CL, &NC);
+  }
+  if (CL < 1 || CL > 16 || NC < 1 || (long long)CL * NC > m.npieces) {
+    set_error("cluster=%d clusters=%d invalid for %d pieces", CL, NC, m.npieces);
+    return TR_ERR_INVALID;
+  }
+  g->CL = CL;
+  g->NC = NC;
+  const int NJ = CL * NC;
+  const int max_np = ceil_div(m.npieces, NJ);
+  SlabSmem sm{};
+  bool ok = false;
+  const int nb1_opts[4] = {c.R * l.NSL, 4, 3, 2};
+  const int nb3_opts[4] = {max_np, 16, 8, 4};
+  for (int na2 = 4; na2 >= 2 && !ok; --na2) {
+    for (int na3 = 2; na3 >= 1 && !ok; --na3) {
+      for (int i1 = 0; i1 < 4 && !ok; ++i1) {
+        const int nb1 = nb1_opts[i1];
+        if (i1 > 0 && nb1 >= c.R * l.NSL) continue;
+        for (int i3 = 0; i3 < 4 && !ok; ++i3) {
+          const int nb3 = nb3_opts[i3];
+          if (i3 == 0 && max_np > 64) continue;
+          if (i3 > 0 && nb3 >= max_np) continue;
+          sm = slab_smem(p, l, na2, na3, nb1, nb3);
+          if (sm.total <= p.smem_optin) {
+            ok = true;
+            g->NA2 = na2;
+            g->NA3 = na3;
+            g->NB1 = nb1;
+            g->b1_all = i1 == 0;
+            g->NB3 = nb3;
+            g->b3_all = i3 == 0;
+          }
+        }
+      }
+    }
+  }
+  if (!ok) {
+    set_error("slab kernel needs %zu bytes of shared memory (device allows %zu)", sm.total,
+              p.smem_optin);
+    return TR_ERR_UNSUPPORTED;
+  }
+  g->ystr = tc_ystr(p, l.O2G);
+  g->a2_bytes = sm.a2_bytes;
+  g->a3_bytes = sm.a3_bytes;
+  g->a1_bytes = sm.a1_bytes;
+  g->off_a2 = sm.off_a2;
+  g->off_b2 = sm.off_b2;
+  g->off_a3 = sm.off_a3;
+  g->off_a1 = sm.off_a1;
+  g->off_g1 = sm.off_g1;
+  g->off_b3 = sm.off_b3;
+  g->off_bar = sm.off_bar;
+  // At least 120 KB, so no two CTAs share an SM: a CTA that holds TMEM and waits at the cluster
+  // barrier must never block a cluster peer inside tcgen05.alloc on the same SM.
+  g->smem = std::max<size_t>(sm.total, 120 * 1024);
+  const size_t slot_elems = (size_t)128 * l.O2G * c.O3;
+  const size_t counters = align_up((size_t)g->ntiles * l.NG * CL * sizeof(int), 256);
+  const size_t slots =
+      NC > 1 ? align_up((size_t)g->ntiles * l.NG * NC * slot_elems * sizeof(float), 256) : 0;
+  g->part_elems = (size_t)g->TT * c.O1 * g->ystr;
+  g->parts_off = 256 + counters + slots;
+  const size_t parts =
+      CL > 1 ? (size_t)g->ntiles * l.NG * CL * NC * g->part_elems * sizeof(float) : 0;
+  g->ws_bytes = g->parts_off + parts;
+  return TR_OK;
+}
+
 // Which kernel serves `T` tokens on this plan.
 static int pick_kind(const Plan& p, int64_t T, const tr_tiling* f) {
   if (f && f->kernel != KIND_AUTO) return f->kernel;
@@ -570,6 +801,8 @@ static int pick_kind(const Plan& p, int64_t T, const tr_tiling* f) {
       return KIND_DECODE;
     TcGeom tg;
     if (T >= 1 && p.tc_ok && resolve_tc_geom(p, T, nullptr, &tg) == TR_OK) return KIND_TC05;
+    SlabGeom sg;
+    if (T >= 1 && p.slab_ok && resolve_slab_geom(p, T, nullptr, &sg) == TR_OK) return KIND_SLAB;
     return KIND_MMA;
   }
   return KIND_GENERIC;
@@ -589,6 +822,7 @@ struct GeomCacheEntry {
   trr::MmaGeom g;
   trr::DecodeGeom dg;
   trr::TcGeom tg;
+  trr::SlabGeom lg;
 };
 
 struct tr_plan : public trr::Plan {
@@ -682,6 +916,7 @@ int tr_plan_create(const tr_spec* spec, int32_t dtype, int32_t device, tr_plan**
   p->smem_optin = (size_t)optin;
   query_max_clusters(device, nsm, p->max_clusters);
   p->tc_ok = 0;
+  p->slab_ok = 0;
   if (p->mma_ok) build_tc_layout(p);
   if (p->tc_ok) {
     p->packed_bytes =
@@ -690,6 +925,14 @@ int tr_plan_create(const tr_spec* spec, int32_t dtype, int32_t device, tr_plan**
     p->packed_bytes = align_up(p->m.off_g3 + p->m.bytes_g3, 256);
   } else {
     p->packed_bytes = align_up(p->g.off_g3 + p->g.elems_g3 * elem_size(dtype), 256);
+  }
+  if (p->mma_ok) build_slab_layout(p);
+  if (p->slab_ok) {  // the slab operands follow the others
+    SlabLayout& l = p->sl;
+    l.off_b1 = p->packed_bytes;
+    l.off_b2 = align_up(l.off_b1 + (size_t)p->c.R * l.NSL * l.bytes_b1, 256);
+    l.off_b3 = align_up(l.off_b2 + (size_t)l.NG * l.bytes_b2, 256);
+    p->packed_bytes = align_up(l.off_b3 + (size_t)p->m.npieces * l.bytes_b3, 256);
   }
   *out = p;
   return TR_OK;
@@ -716,10 +959,10 @@ int tr_plan_flops_per_token(const tr_plan* plan, double* flops) {
 }
 
 static int resolve_geom(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling, int* kind,
-                        MmaGeom* g, DecodeGeom* dg, TcGeom* tg);
+                        MmaGeom* g, DecodeGeom* dg, TcGeom* tg, SlabGeom* lg);
 
 static int geom_for(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling, int* kind,
-                    MmaGeom* g, DecodeGeom* dg, TcGeom* tg) {
+                    MmaGeom* g, DecodeGeom* dg, TcGeom* tg, SlabGeom* lg) {
   if (!plan) {
     set_error("null plan");
     return TR_ERR_INVALID;
@@ -736,10 +979,11 @@ static int geom_for(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling
       *g = e.g;
       *dg = e.dg;
       *tg = e.tg;
+      *lg = e.lg;
       return TR_OK;
     }
   }
-  const int st = resolve_geom(plan, tokens, tiling, kind, g, dg, tg);
+  const int st = resolve_geom(plan, tokens, tiling, kind, g, dg, tg, lg);
   if (st == TR_OK && !tiling && tokens > 0) {
     std::lock_guard<std::mutex> lock(plan->cache_mu);
     GeomCacheEntry& e = plan->cache[(uint64_t)tokens % 32];
@@ -748,12 +992,13 @@ static int geom_for(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling
     e.g = *g;
     e.dg = *dg;
     e.tg = *tg;
+    e.lg = *lg;
   }
   return st;
 }
 
 static int resolve_geom(const tr_plan* plan, int64_t tokens, const tr_tiling* tiling, int* kind,
-                        MmaGeom* g, DecodeGeom* dg, TcGeom* tg) {
+                        MmaGeom* g, DecodeGeom* dg, TcGeom* tg, SlabGeom* lg) {
   *kind = pick_kind(*plan, tokens, tiling);
   if (*kind == KIND_MMA) {
     if (tokens == 0) {
@@ -777,6 +1022,12 @@ static int resolve_geom(const tr_plan* plan, int64_t tokens, const tr_tiling* ti
     if (tokens == 0) return TR_OK;
     return resolve_tc_geom(*plan, tokens, tiling, tg);
   }
+  if (*kind == KIND_SLAB) {
+    memset(g, 0, sizeof(*g));
+    memset(lg, 0, sizeof(*lg));
+    if (tokens == 0) return TR_OK;
+    return resolve_slab_geom(*plan, tokens, tiling, lg);
+  }
   set_error("kernel kind %d not available in this build", *kind);
   return TR_ERR_UNSUPPORTED;
 }
@@ -791,9 +1042,13 @@ int tr_workspace_bytes_tiled(const tr_plan* plan, int64_t tokens, const tr_tilin
   MmaGeom g;
   DecodeGeom dg;
   TcGeom tg;
-  const int st = geom_for(plan, tokens, tiling, &kind, &g, &dg, &tg);
+  SlabGeom lg;
+  const int st = geom_for(plan, tokens, tiling, &kind, &g, &dg, &tg, &lg);
   if (st != TR_OK) return st;
-  *bytes = kind == KIND_MMA ? g.ws_bytes : kind == KIND_TC05 ? tg.ws_bytes : 0;
+  *bytes = kind == KIND_MMA    ? g.ws_bytes
+           : kind == KIND_TC05 ? tg.ws_bytes
+           : kind == KIND_SLAB ? lg.ws_bytes
+                               : 0;
   return TR_OK;
 }
 
@@ -858,13 +1113,20 @@ int tr_plan_tiling(const tr_plan* plan, int64_t tokens, tr_tiling* out) {
   MmaGeom g;
   DecodeGeom dg;
   TcGeom tg;
-  const int st = geom_for(plan, tokens, nullptr, &kind, &g, &dg, &tg);
+  SlabGeom lg;
+  const int st = geom_for(plan, tokens, nullptr, &kind, &g, &dg, &tg, &lg);
   if (st != TR_OK) return st;
   out->kernel = kind;
   if (kind == KIND_TC05) {
     out->tokens_per_tile = tg.TT;
     out->cluster = tg.CL;
     out->clusters = tg.NC;
+    return TR_OK;
+  }
+  if (kind == KIND_SLAB) {
+    out->tokens_per_tile = lg.TT;
+    out->cluster = lg.CL;
+    out->clusters = lg.NC;
     return TR_OK;
   }
   if (kind == KIND_DECODE) {
@@ -886,7 +1148,8 @@ static int forward_impl(const tr_plan* plan, const void* packed, const void* x, 
   MmaGeom g;
   DecodeGeom dg;
   TcGeom tg;
-  int st = geom_for(plan, tokens, tiling, &kind, &g, &dg, &tg);
+  SlabGeom lg;
+  int st = geom_for(plan, tokens, tiling, &kind, &g, &dg, &tg, &lg);
   if (st != TR_OK) return st;
   if (tokens == 0) return TR_OK;
   if (!packed || !x || !y) {
@@ -899,6 +1162,18 @@ static int forward_impl(const tr_plan* plan, const void* packed, const void* x, 
   }
   if (kind == KIND_GENERIC) return launch_generic(*plan, packed, x, tokens, y, stream, epi);
   if (kind == KIND_DECODE) return launch_decode(*plan, dg, packed, x, tokens, y, stream, epi);
+  if (kind == KIND_SLAB) {
+    if (!workspace || workspace_bytes < lg.ws_bytes) {
+      set_error("workspace of %zu bytes needed, %zu given", lg.ws_bytes,
+                workspace ? workspace_bytes : (size_t)0);
+      return TR_ERR_WORKSPACE;
+    }
+    if ((uintptr_t)workspace & 15) {
+      set_error("workspace must be 16-byte aligned");
+      return TR_ERR_ALIGN;
+    }
+    return launch_slab(*plan, lg, packed, x, tokens, y, workspace, stream, epi);
+  }
   if (kind == KIND_TC05) {
     if (!workspace || workspace_bytes < tg.ws_bytes) {
       set_error("workspace of %zu bytes needed, %zu given", tg.ws_bytes,
@@ -1032,12 +1307,16 @@ int tr_plan_describe(const tr_plan* plan, char* buf, size_t len) {
       "\"canonical_out\": [%d, %d, %d], \"rank\": %d, \"macs_per_token\": %.0f, "
       "\"mma\": %d, \"rank_padded\": %d, \"pieces\": %d, \"packed_bytes\": %zu, "
       "\"dtype\": %d, \"tcgen05\": %d, \"o2_group\": %d, \"groups\": %d, "
-      "\"tmem_cols\": %d, \"d1_buffers\": %d, \"shared_d12\": %d}",
+      "\"tmem_cols\": %d, \"d1_buffers\": %d, \"shared_d12\": %d, \"slab\": %d, "
+      "\"slab_o2_group\": %d, \"slab_groups\": %d, \"slab_d2_buffers\": %d, "
+      "\"rank_slabs\": %d}",
       names[c.role[0]], names[c.role[1]], names[c.role[2]], c.reversed, c.I1, c.I2, c.I3, c.O1,
       c.O2, c.O3, c.R, plan->macs_per_token, plan->mma_ok, m.RP, m.npieces, plan->packed_bytes,
       plan->dtype, plan->tc_ok, plan->tc_ok ? plan->t.O2G : 0, plan->tc_ok ? plan->t.NG : 0,
       plan->tc_ok ? plan->t.tmem_cols : 0, plan->tc_ok ? plan->t.ND1 : 0,
-      plan->tc_ok ? plan->t.shared_d12 : 0);
+      plan->tc_ok ? plan->t.shared_d12 : 0, plan->slab_ok, plan->slab_ok ? plan->sl.O2G : 0,
+      plan->slab_ok ? plan->sl.NG : 0, plan->slab_ok ? plan->sl.ND2 : 0,
+      plan->slab_ok ? plan->sl.NSL : 0);
   if (n < 0 || (size_t)n >= len) {
     set_error("buffer too small");
     return TR_ERR_INVALID;

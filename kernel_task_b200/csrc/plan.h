@@ -71,6 +71,32 @@ struct TcLayout {
   size_t off_b3, bytes_b3_piece;
 };
 
+// Operand layout of the slab kernel (ring_slab.cu): the ring rank u of the first link in NSL
+// slabs of 8 (u = 8 sl + ul), K-major, no swizzle, 8x8 core matrices as above.
+//   B1 per (s, sl):   rows (o1, ul) padded to 16 = N1S, K = K1P (i1)    (S1, dtype E)
+//   B2 per o2 group:  rows (o2 of group, v padded to RV) = N2, K = K2S = NSL * KSL ordered
+//                     (sl, i2, ul), each slab's run padded to KSL = I2*8 rounded up to 16  (fp16)
+//   B3 per piece:     rows o3 padded to 16 = N3P, K = K3P (v padded to 16)   (S3, fp16)
+// TMEM columns of a CTA: D1 x 2 slabs [0, 2 N1S), D2 x ND2 [d2_col, + ND2 N2),
+// D3 [d3_col, + O2G N3P).
+struct SlabLayout {
+  int NSL;       // rank slabs of 8
+  int RV;        // the rank padded to a multiple of 8 (v, the S2 columns per o2)
+  int N1S;       // O1 * 8 padded to 16: S1 N per slab, D1 columns per slab buffer
+  int KSL;       // I2 * 8 padded to 16: S2 K per slab
+  int K2S;       // NSL * KSL
+  int O2G, NG;   // o2 modes per group, groups
+  int N2;        // O2G * RV (S2 N, D2 columns)
+  int ND2;       // D2 buffers (2: S2 of the next piece overlaps C2; 1: wider groups)
+  int N3P;       // O3 padded to 16 (S3 N per o2)
+  int K3P;       // RV padded to 16 (S3 K)
+  int d2_col, d3_col;
+  int tmem_cols;
+  size_t off_b1, bytes_b1;  // per (s, slab)
+  size_t off_b2, bytes_b2;  // per o2 group
+  size_t off_b3, bytes_b3;  // per piece
+};
+
 // Canonical cores in natural [l][o][i][r] order (generic CUDA-core kernel, ring_generic.cu).
 struct GenericLayout {
   size_t off_g1, off_g2, off_g3;
@@ -82,7 +108,8 @@ enum KernelKind {
   KIND_GENERIC = 1,
   KIND_MMA = 2,
   KIND_TC05 = 3,
-  KIND_DECODE = 4
+  KIND_DECODE = 4,
+  KIND_SLAB = 5
 };
 
 struct Plan {
@@ -93,8 +120,10 @@ struct Plan {
   double macs_per_token;  // chosen order, multiply-adds per token
   int mma_ok;             // the mma.sync kernel handles this shape and dtype
   int tc_ok;              // the tcgen05 kernel handles it (its operands are packed too)
+  int slab_ok;            // the slab kernel handles it (its operands are packed too)
   MmaLayout m;
   TcLayout t;
+  SlabLayout sl;
   GenericLayout g;
   size_t packed_bytes;
   int num_sms;
@@ -163,6 +192,23 @@ struct TcGeom {
   size_t ws_bytes;
 };
 
+// Geometry of one slab-kernel launch: row tiles of TT tokens x NG o2 groups x NJ = CL * NC
+// CTAs splitting the pieces.
+struct SlabGeom {
+  int TT, ntiles;
+  int CL, NC;
+  int NA2, NA3;        // A2 slab slots, A3 buffers
+  int NB1, b1_all;     // B1 slab-slice slots; b1_all: all R * NSL slices loaded once
+  int NB3, b3_all;     // B3 slots; b3_all: the CTA's whole piece range loaded once
+  int ystr;            // row stride (floats) of the partial y in shared memory
+  size_t a2_bytes, a3_bytes, a1_bytes;
+  size_t off_a2, off_b2, off_a3, off_a1, off_g1, off_b3, off_bar;
+  size_t smem;
+  size_t part_elems;   // floats of one CTA's partial sums in the workspace (CL > 1)
+  size_t parts_off;    // workspace offset of the per-CTA partial sums
+  size_t ws_bytes;
+};
+
 // What a kernel writes for output element y[i] = v (v: the fp32 sum of the ring pieces):
 //   kind 0: v;  kind 1: aux[i] + v (residual add);  kind 2: silu(aux[i]) * v (gated MLP);
 // stored as fp32 when out_f32, else in the plan's element type.  aux is [T, d_out] row-major,
@@ -191,6 +237,9 @@ int forward_noalloc(const Plan& p, const void* packed, const void* x, int64_t T,
 int resolve_decode_geom(const Plan& p, int64_t T, const tr_tiling* force, DecodeGeom* g);
 int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* force, TcGeom* g);
 int launch_tc05(const Plan& p, const TcGeom& g, const void* packed, const void* x, int64_t T,
+                void* y, void* ws, void* stream, const Epi& epi);
+int resolve_slab_geom(const Plan& p, int64_t T, const tr_tiling* force, SlabGeom* g);
+int launch_slab(const Plan& p, const SlabGeom& g, const void* packed, const void* x, int64_t T,
                 void* y, void* ws, void* stream, const Epi& epi);
 int decode_variant(const Plan& p);
 int decode_max_threads(int variant, int mt2);

@@ -67,4 +67,10 @@ struct FixedShape {
   X(16, 16, 16, 16, 28, 32, 16, 0, 1)        \
   X(16, 28, 32, 16, 16, 16, 16, 2, 1)
 
+// The slab kernel also compiles the config-3 shape (rank 32, which the other tcgen05 kernel does
+// not take).
+#define TRR_SLAB_SHAPES(X) \
+  TRR_FIXED_SHAPES(X)      \
+  X(16, 16, 16, 16, 28, 32, 32, 0, 1)
+
 }  // namespace trr

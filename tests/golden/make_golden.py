@@ -118,11 +118,11 @@ def main() -> None:
 
     np.savez_compressed(HERE / "reference_vectors.npz", **out)
 
-    # 5. BASELINE configs 3-5 (bf16): cores from kernel_task_b200.spec.baseline_cores (seeded,
+    # 5. The benchmark configs 3-5 (bf16): cores from kernel_task_b200.spec.baseline_cores (seeded,
     #    CPU generator), fingerprinted by sha256; y = the reference's contraction in fp32 of the
     #    bf16 values, for a few tokens.  Stored: hashes + x + y (cores are regenerated).
     big = {}
-    cfgs = {"c3": (kspec.SPEC_C3, (1, 2)), "c5": (kspec.SPEC_C5, (1, 2))}
+    cfgs = {"c3": (kspec.SPEC_C3, (1, 2, 8)), "c5": (kspec.SPEC_C5, (1, 2))}
     cfgs.update({f"c4_{n}": (s, (1,)) for n, s in kspec.SPEC_C4.items() if n in
                  ("q", "k", "gate", "down")})
     bmeta = {}

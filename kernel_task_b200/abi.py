@@ -17,7 +17,7 @@ TR_ERR_CUDA = -4
 TR_ERR_ALIGN = -5
 TR_ERR_TIMEOUT = -6
 TR_F32, TR_F16, TR_BF16 = 0, 1, 2
-KERNEL_AUTO, KERNEL_GENERIC, KERNEL_MMA, KERNEL_TC05, KERNEL_DECODE = 0, 1, 2, 3, 4
+KERNEL_AUTO, KERNEL_GENERIC, KERNEL_MMA, KERNEL_TC05, KERNEL_DECODE, KERNEL_SLAB = 0, 1, 2, 3, 4, 5
 TR_EPI_NONE, TR_EPI_ADD, TR_EPI_SILU_MUL = 0, 1, 2
 
 

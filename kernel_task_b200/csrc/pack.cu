@@ -181,11 +181,11 @@ __global__ void pack_tc_kernel(CoreView<E> c0, CoreView<E> c1, CoreView<E> c2, T
 }
 
 struct SlabPackDims {
-  int I1, I2, I3, O1, O2, O3, R, K1P, NSL, RV, N1S, KSL, K2S, O2G, N2, N3P, K3P, npieces;
+  int I1, I2, I3, O1, O2, O3, R, K1P, SW, NSL, RV, N1S, KSL, K2S, O2G, N2, N3P, K3P, npieces;
 };
 
 // Slab-kernel operands (ring_slab.cu): B1 per (s, sl) [N1S rows (o1, ul)] x [K1P i1] in the input
-// dtype E, with u = 8 sl + ul; B2 per o2 group [N2 rows (o2, v)] x [K2S (sl, i2, ul)] and B3 per
+// dtype E, with u = SW sl + ul; B2 per o2 group [N2 rows (o2, v)] x [K2S (sl, i2, ul)] and B3 per
 // piece [N3P rows o3] x [K3P v] in fp16; zero where a padded index has no core entry.
 template <typename E>
 __global__ void pack_slab_kernel(CoreView<E> c0, CoreView<E> c1, CoreView<E> c2, SlabPackDims d,
@@ -201,7 +201,7 @@ __global__ void pack_slab_kernel(CoreView<E> c0, CoreView<E> c1, CoreView<E> c2,
       q /= d.N1S;
       const int sl = (int)(q % d.NSL);
       const int s = (int)(q / d.NSL);
-      const int o1 = n / 8, u = 8 * sl + n % 8;
+      const int o1 = n / d.SW, ul = n % d.SW, u = d.SW * sl + ul;
       const float v = (o1 < d.O1 && u < d.R && k < d.I1) ? c0.at(s, o1, k, u) : 0.f;
       *reinterpret_cast<E*>(b1 + ((size_t)s * d.NSL + sl) * d.N1S * d.K1P * sizeof(E) +
                             umma_kmajor_offset(n, k, d.K1P)) = from_f32<E>(v);
@@ -217,7 +217,7 @@ __global__ void pack_slab_kernel(CoreView<E> c0, CoreView<E> c1, CoreView<E> c2,
       const int grp = (int)(q / d.N2);
       const int o2 = grp * d.O2G + n / d.RV, vv = n % d.RV;
       const int sl = k / d.KSL, kk = k % d.KSL;
-      const int i2 = kk / 8, u = 8 * sl + kk % 8;
+      const int i2 = kk / d.SW, u = d.SW * sl + kk % d.SW;
       v = (o2 < d.O2 && vv < d.R && i2 < d.I2 && u < d.R) ? c1.at(u, o2, i2, vv) : 0.f;
       dst = b2 + (size_t)grp * d.N2 * d.K2S * 2 + umma_kmajor_offset(n, k, d.K2S);
     } else {
@@ -276,7 +276,7 @@ static int pack_typed(const Plan& p, const void* const cores[3], void* packed, c
       }
       if (p.slab_ok) {
         const SlabLayout& l = p.sl;
-        SlabPackDims sd{c.I1, c.I2, c.I3, c.O1, c.O2, c.O3, c.R, m.K1P, l.NSL, l.RV, l.N1S,
+        SlabPackDims sd{c.I1, c.I2, c.I3, c.O1, c.O2, c.O3, c.R, m.K1P, l.SW, l.NSL, l.RV, l.N1S,
                         l.KSL, l.K2S, l.O2G, l.N2, l.N3P, l.K3P, m.npieces};
         const size_t sn1 = (size_t)c.R * l.NSL * l.N1S * m.K1P;
         const size_t sn2 = (size_t)l.NG * l.N2 * l.K2S;

@@ -239,64 +239,84 @@ static SlabSmem slab_smem(const Plan& p, const SlabLayout& l, int NA2, int NA3, 
   return s;
 }
 
-// Slab-kernel operand layout (appended after the other packed layouts).  O2 is split into NG
-// groups so that a CTA's TMEM holds two D1 slab buffers, ND2 D2 buffers and the S3 accumulators
-// of its group within 512 columns, and its operands fit in shared memory; of the two D2 depths
-// the one giving fewer groups wins (less repeated S1 and C1 work), two buffers on a tie.
-// Needs ranks <= 32, O1 <= 32 (one D1 slab of at most 256 columns) and fp16/bf16.
+// Which D2 depth the slab layout prefers: 0 the one giving fewer o2 groups (two buffers on a
+// tie), 1 one buffer, 2 two buffers whenever a group fits with them.
+#ifndef TRR_SLAB_D2_RULE
+#define TRR_SLAB_D2_RULE 0
+#endif
+
+// Slab-kernel operand layout (appended after the other packed layouts).  The ring rank u of the
+// first link is cut into NSL slabs of SW = 8 or 4 ranks.  O2 is split into NG groups so that a
+// CTA's TMEM holds two D1 slab buffers (2 * O1 * SW columns), ND2 D2 buffers and the S3
+// accumulators of its group within 512 columns, and its operands fit in shared memory.  Of the
+// (SW, D2 depth) choices the one with the fewest groups wins (each group repeats S1 and C1):
+// slabs of 4 halve D1 and so widen the groups where D1 binds TMEM (config 5: groups of 7 instead
+// of 5); SW = 8 and two D2 buffers on ties (fewer slab steps; S2 of the next piece overlaps C2).
+// The D2 depth follows TRR_SLAB_D2_RULE.  Needs ranks <= 32, O1 * SW <= 256 and fp16/bf16.
 static void build_slab_layout(Plan* p) {
   const Canon& c = p->c;
   SlabLayout& l = p->sl;
   p->slab_ok = 0;
   if (p->dtype == TR_F32 || c.R > 32 || c.O1 > 32 || c.I2 > 128) return;
-  l.NSL = ceil_div(c.R, 8);
-  l.RV = 8 * l.NSL;
-  l.N1S = ceil_div(c.O1 * 8, 16) * 16;
-  l.KSL = ceil_div(c.I2 * 8, 16) * 16;
-  l.K2S = l.NSL * l.KSL;
-  l.N3P = ceil_div(c.O3, 16) * 16;
-  l.K3P = std::max(16, ceil_div(l.RV, 16) * 16);
-  if (l.N3P > 256) return;
-  // the last TMEM column a C1 warp reads (16-column loads from the start of its o1 half)
-  const int h = (c.O1 + 1) / 2;
-  const int c1_reach = l.N1S + std::max(ceil_div(h * 8, 16) * 16,
-                                        h * 8 + ceil_div((c.O1 - h) * 8, 16) * 16);
-  const int step = (l.RV % 16 == 0) ? 1 : 2;  // S2's N = O2G * RV must be a multiple of 16
-  auto tmem_need = [&](int nd2, int o2g) {
-    return std::max(2 * l.N1S + nd2 * o2g * l.RV + o2g * l.N3P, c1_reach);
-  };
-  auto fits = [&](int nd2, int o2g) {
-    SlabLayout t = l;
-    t.O2G = o2g;
-    t.N2 = o2g * l.RV;
-    t.ND2 = nd2;
-    return tmem_need(nd2, o2g) <= 512 && slab_smem(*p, t, 2, 1, 2, 4).total <= p->smem_optin;
-  };
-  int best_nd2 = 0, best_w = 0, best_ng = 0;
-  for (int nd2 = 2; nd2 >= 1; --nd2) {
-    int o2g = std::min(ceil_div(c.O2, step) * step, 256 / l.RV);
-    o2g -= o2g % step;
-    while (o2g >= step && !fits(nd2, o2g)) o2g -= step;
-    if (o2g < step) continue;
-    int w = ceil_div(c.O2, ceil_div(c.O2, o2g));  // balanced width, same group count
-    if (w % step) w += step - w % step;
-    w = std::min(w, o2g);
-    const int ng = ceil_div(c.O2, w);
-    if (best_nd2 == 0 || ng < best_ng) {
-      best_nd2 = nd2;
-      best_w = w;
-      best_ng = ng;
+  SlabLayout best{};
+  int best_need = 0;
+  // slabs of 4 would halve D1 and widen the groups (config 5: 4 groups of 7 instead of 6 of 5),
+  // but a slab step costs about the same whatever its size and they double the steps: measured
+  // slower (config 5 28.8 against 26.3 ms at 8192 tokens, config 3 T = 256 8.1 against 6.1 ms),
+  // so the layout keeps SW = 8 (the kernel handles both)
+  for (int sw = 8; sw >= 8; sw /= 2) {
+    SlabLayout t{};
+    t.SW = sw;
+    t.NSL = ceil_div(c.R, sw);
+    t.RV = 8 * ceil_div(c.R, 8);
+    t.N1S = ceil_div(c.O1 * sw, 16) * 16;
+    t.KSL = ceil_div(c.I2 * sw, 16) * 16;
+    t.K2S = t.NSL * t.KSL;
+    t.N3P = ceil_div(c.O3, 16) * 16;
+    t.K3P = std::max(16, ceil_div(t.RV, 16) * 16);
+    if (t.N3P > 256 || t.N1S > 256) continue;
+    // the last TMEM column a C1 warp reads (16-column loads from the start of its o1 half)
+    const int h = (c.O1 + 1) / 2;
+    const int c1_reach = t.N1S + std::max(ceil_div(h * sw, 16) * 16,
+                                          h * sw + ceil_div((c.O1 - h) * sw, 16) * 16);
+    const int step = (t.RV % 16 == 0) ? 1 : 2;  // S2's N = O2G * RV must be a multiple of 16
+    auto tmem_need = [&](int nd2, int o2g) {
+      return std::max(2 * t.N1S + nd2 * o2g * t.RV + o2g * t.N3P, c1_reach);
+    };
+    auto fits = [&](int nd2, int o2g) {
+      SlabLayout u = t;
+      u.O2G = o2g;
+      u.N2 = o2g * t.RV;
+      u.ND2 = nd2;
+      return tmem_need(nd2, o2g) <= 512 && slab_smem(*p, u, 2, 1, 2, 4).total <= p->smem_optin;
+    };
+    for (int nd2 = 2; nd2 >= 1; --nd2) {
+      if (TRR_SLAB_D2_RULE == 1 && nd2 == 2) continue;
+      int o2g = std::min(ceil_div(c.O2, step) * step, 256 / t.RV);
+      o2g -= o2g % step;
+      while (o2g >= step && !fits(nd2, o2g)) o2g -= step;
+      if (o2g < step) continue;
+      int w = ceil_div(c.O2, ceil_div(c.O2, o2g));  // balanced width, same group count
+      if (w % step) w += step - w % step;
+      w = std::min(w, o2g);
+      const int ng = ceil_div(c.O2, w);
+      if (TRR_SLAB_D2_RULE == 2 && best.ND2 == 2 && best.SW == sw) continue;
+      if (best.NG == 0 || ng < best.NG) {
+        best = t;
+        best.ND2 = nd2;
+        best.O2G = w;
+        best.NG = ng;
+        best.N2 = w * t.RV;
+        best_need = tmem_need(nd2, w);
+      }
     }
   }
-  if (best_nd2 == 0) return;
-  l.ND2 = best_nd2;
-  l.O2G = best_w;
-  l.NG = best_ng;
-  l.N2 = l.O2G * l.RV;
+  if (best.NG == 0) return;
+  l = best;
   l.d2_col = 2 * l.N1S;
   l.d3_col = l.d2_col + l.ND2 * l.N2;
   l.tmem_cols = 32;
-  while (l.tmem_cols < tmem_need(l.ND2, l.O2G)) l.tmem_cols *= 2;
+  while (l.tmem_cols < best_need) l.tmem_cols *= 2;
   l.bytes_b1 = (size_t)l.N1S * p->m.K1P * elem_size(p->dtype);
   l.bytes_b2 = (size_t)l.N2 * l.K2S * 2;
   l.bytes_b3 = (size_t)l.N3P * l.K3P * 2;
@@ -799,9 +819,16 @@ static int pick_kind(const Plan& p, int64_t T, const tr_tiling* f) {
     // on c1/c2 it takes half the tcgen05 kernel's time (c2 T = 2: 14.5 against 26.8 us cold)
     if (T >= 1 && T * p.c.O1 <= 32 && resolve_decode_geom(p, T, nullptr, &d) == TR_OK)
       return KIND_DECODE;
+    // the slab kernel where the tcgen05 kernel does not take the spec (ranks above 16), or where
+    // its layout needs at least a quarter fewer o2 groups (each group repeats S1 and C1): config
+    // 4 q/o at T = 256 measured 363 us against 532 us; on equal groups the tcgen05 kernel's
+    // whole-piece stages win (c2 T = 256: 187 us against 250 us)
+    const bool slab_first =
+        p.slab_ok && (!p.tc_ok || (long long)p.sl.NG * 4 <= (long long)p.t.NG * 3);
     TcGeom tg;
-    if (T >= 1 && p.tc_ok && resolve_tc_geom(p, T, nullptr, &tg) == TR_OK) return KIND_TC05;
     SlabGeom sg;
+    if (T >= 1 && slab_first && resolve_slab_geom(p, T, nullptr, &sg) == TR_OK) return KIND_SLAB;
+    if (T >= 1 && p.tc_ok && resolve_tc_geom(p, T, nullptr, &tg) == TR_OK) return KIND_TC05;
     if (T >= 1 && p.slab_ok && resolve_slab_geom(p, T, nullptr, &sg) == TR_OK) return KIND_SLAB;
     return KIND_MMA;
   }

@@ -72,18 +72,19 @@ struct TcLayout {
 };
 
 // Operand layout of the slab kernel (ring_slab.cu): the ring rank u of the first link in NSL
-// slabs of 8 (u = 8 sl + ul), K-major, no swizzle, 8x8 core matrices as above.
+// slabs of SW = 8 or 4 ranks (u = SW sl + ul), K-major, no swizzle, 8x8 core matrices as above.
 //   B1 per (s, sl):   rows (o1, ul) padded to 16 = N1S, K = K1P (i1)    (S1, dtype E)
 //   B2 per o2 group:  rows (o2 of group, v padded to RV) = N2, K = K2S = NSL * KSL ordered
-//                     (sl, i2, ul), each slab's run padded to KSL = I2*8 rounded up to 16  (fp16)
+//                     (sl, i2, ul), each slab's run padded to KSL = I2*SW rounded up to 16 (fp16)
 //   B3 per piece:     rows o3 padded to 16 = N3P, K = K3P (v padded to 16)   (S3, fp16)
 // TMEM columns of a CTA: D1 x 2 slabs [0, 2 N1S), D2 x ND2 [d2_col, + ND2 N2),
 // D3 [d3_col, + O2G N3P).
 struct SlabLayout {
-  int NSL;       // rank slabs of 8
+  int SW;        // ranks per slab: 8 or 4
+  int NSL;       // rank slabs
   int RV;        // the rank padded to a multiple of 8 (v, the S2 columns per o2)
-  int N1S;       // O1 * 8 padded to 16: S1 N per slab, D1 columns per slab buffer
-  int KSL;       // I2 * 8 padded to 16: S2 K per slab
+  int N1S;       // O1 * SW padded to 16: S1 N per slab, D1 columns per slab buffer
+  int KSL;       // I2 * SW padded to 16: S2 K per slab
   int K2S;       // NSL * KSL
   int O2G, NG;   // o2 modes per group, groups
   int N2;        // O2G * RV (S2 N, D2 columns)

@@ -1,11 +1,11 @@
 // Tensor-ring kernel on the 5th-generation tensor cores for ranks up to 32 and for large token
-// counts: the ring rank is cut into slabs of eight, and the first two stages advance slab by
-// slab.  One launch per call; every contraction runs as tcgen05.mma with operands in shared
+// counts: the ring rank is cut into slabs of SW = 8 or 4 ranks, and the first two stages
+// advance slab by slab.  One launch per call; every contraction runs as tcgen05.mma with operands in shared
 // memory and accumulators in TMEM.
 //
 // Per CTA: one row tile of TT tokens, one group of O2G output modes o2 and a contiguous range of
-// ring pieces (i3, s).  Each piece's rank index u of the first link runs over NSL slabs of 8
-// (u = 8 sl + ul); slab step g = j NSL + sl of piece j:
+// ring pieces (i3, s).  Each piece's rank index u of the first link runs over NSL slabs of SW
+// (u = SW sl + ul); slab step g = j NSL + sl of piece j:
 //   S1  D1[g&1][(t,i2), (o1,ul)] = A1[(t,i2), i1] . B1_{s,sl}[(o1,ul), i1]     A1 = x slice of i3
 //   C1  D1 -> A2 slot g%NA2 [(t,o1), (i2,ul)] (fp16): the transpose between S1's rows and S2's
 //       rows, TMEM -> registers -> shared memory, one D1 row (t,i2) per thread
@@ -13,19 +13,23 @@
 // and once per piece:
 //   C2  D2 -> A3[o2][(t,o1), v] (fp16)
 //   S3  D3[o2][(t,o1), o3] += A3[o2] . B3_piece[o3, v]                 (accumulated over pieces)
-// D1 holds two slabs (2 * 8 O1 TMEM columns), so S1 of slab g+2 runs while C1 converts slab
+// D1 holds two slabs (2 * SW * O1 TMEM columns), so S1 of slab g+2 runs while C1 converts slab
 // g+1, and S2 consumes each A2 slab as soon as it is written: the S1 -> C1 -> S2 chain overlaps
-// across slabs instead of serialising per piece, at the TMEM cost of a quarter (rank 32) or half
-// (rank 16) of a whole-piece D1.
-// Roles (480 threads), as in the tcgen05 kernel of ring_tc05.cu:
+// across slabs instead of serialising per piece, at a fraction of a whole-piece D1's TMEM (the
+// rest widens the o2 groups).  C1 stores one 16-byte chunk (SW 8) or half a chunk (SW 4) per o1.
+// Roles (512 threads):
 //   warps 0-7   C1 (warps w and w+4 read the same TMEM lanes, each half of the o1 range)
 //   warps 8-11  C2, and the D3 read-out with warps 0-7 after the last piece
-//   warp 12     issuer A: S1 of slab g+2 once C1 read slab g, S2 of slab g once C1 wrote it
-//   warp 13     issuer B: S3 of each piece
-//   warp 14     feeder: B2 once, B1 slab slices and B3 by TMA bulk copy (all at once when they
+//   warp 12     S1 issuer: S1 of slab g once C1 has read slab g - 2 (its D1 buffer)
+//   warp 13     S2 issuer: S2 of slab g once C1 has written it
+//   warp 14     S3 issuer: S3 of each piece
+//   warp 15     feeder: B2 once, B1 slab slices and B3 by TMA bulk copy (all at once when they
 //               fit, else rings refilled as the tensor-core stages release slots), and the x
 //               slice A1 of each further i3 (the first two are staged by the converter and
 //               feeder warps)
+// One issuing warp per stage: an issuer that waits (S2 on C2 reading D2, S3 on C2) holds up no
+// other stage; measured with per-step clock marks, a single S1+S2 issuer held C1 idle most of
+// each slab step behind S2's waits.
 // Hand-offs are mbarriers: tcgen05.commit arrivals from the issuers (S1DONE, S2SL, S2DONE,
 // S3DONE) and one arrival per converter warp (D1READ: its TMEM loads landed, the buffer may be
 // overwritten; C1DONE / C2DONE: its operand slab is written).  Ring depths are chosen so that no
@@ -59,7 +63,7 @@ namespace cg = cooperative_groups;
 
 namespace trr {
 
-constexpr int kSlThreads = 480;
+constexpr int kSlThreads = 512;
 constexpr int kSlBuildThreads = 416;  // converter and feeder warps: first x slices
 constexpr int kSlBarBuild = 1;        // named barrier of the first x slices (0 is __syncthreads)
 constexpr unsigned kSlPollLimit = 1u << 24;  // feeder polls without progress before it gives up
@@ -80,8 +84,8 @@ enum {
   SB_B3FULL = 44,  // [16] B3 landed (slot 0 only when the whole range loads at once)
   SB_B2FULL = 60,  // B2 landed
   SB_D3DONE = 61,  // commit after the last S3: every tensor-core operation completed
-  SB_DRAIN = 62,   // [2] after the piece loop: the two issuing warps' own work completed
-  SB_COUNT = 64
+  SB_DRAIN = 62,   // [3] after the piece loop: each issuing warp's own work completed
+  SB_COUNT = 65
 };
 
 template <class S>
@@ -97,7 +101,7 @@ struct SlabParams {
   int* status;
   float* parts;    // per-CTA partial sums in the workspace (CL > 1)
   int T, TT, CL, NC, NG, O2G;
-  int NSL, N1S, KSS, K2S, RV, N2, ND2, N3P, K3P, d2_col, d3_col, tmem_cols;
+  int SW, NSL, N1S, KSS, K2S, RV, N2, ND2, N3P, K3P, d2_col, d3_col, tmem_cols;
   int b1_bytes, b2_bytes, b3_bytes;
   int off_a2, off_b2, off_a3, off_a1, off_g1, off_b3, off_bar;
   int NA2, a2_bytes, NA3, a3_bytes, a1_bytes, NB1, b1_all, NB3, b3_all;
@@ -271,25 +275,34 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
   };
 
   if (warp == 12) {
-    // ===================== issuer A: S1 and S2, slab by slab ==================================
-    // The whole warp runs the loop (uniform decisions); one elected lane issues.
+    // ===================== S1 issuer: S1 of slab g once C1 read slab g - 2 ====================
+    // The whole warp runs the loop (uniform decisions); one elected lane issues.  S1 runs ahead
+    // of S2 on its own: C1 is fed at its own pace, whatever S2 and C2 wait for.
+    pdl_wait();
+    bool ok = true;
+    for (int g = 0; g < G && ok; ++g) {
+      if (g >= 2) {  // the D1 slab buffer of g was read by C1 (slab g - 2)
+        ok = warp_wait(bar(SB_D1READ + (g & 1)), ((g - 2) >> 1) & 1, abort, lim);
+        tc_fence_after();
+      }
+      if (ok) ok = issue_s1(g);
+    }
+    // Drain this warp's tensor-core work before the CTA barrier that precedes the TMEM release,
+    // whatever happened (another warp may raise the abort flag after the last MMA was issued).
+    commit_one(bar(SB_DRAIN));
+    if (lane == 0) mbar_drain_spin(bar(SB_DRAIN), 0);
+    __syncwarp();
+  } else if (warp == 13) {
+    // ===================== S2 issuer: S2 of slab g once C1 wrote its A2 slot ==================
     pdl_wait();
     bool ok = true, b2ok = false;
-    for (int g = 0; g < 2 && g < G && ok; ++g) ok = issue_s1(g);
     const uint32_t sbo2 = (uint32_t)(p.K2S / 8) * 128;
     const uint32_t idesc2 = umma_idesc<__half>(128, p.N2);
     for (int g = 0; g < G; ++g) {
       const int j = g / NSL, sl = g - j * NSL;
-      // ---- S1(g + 2) into the D1 slab buffer C1 has just read
-      if (ok && g + 2 < G) {
-        ok = warp_wait(bar(SB_D1READ + (g & 1)), (g >> 1) & 1, abort, lim);
-        tc_fence_after();
-        if (ok) ok = issue_s1(g + 2);
-      }
-      // ---- S2 slab g: C1 wrote its A2 slot; the D2 buffer's previous piece was read by C2
       if (ok) ok = warp_wait(bar(SB_C1DONE + (g & 3)), (g >> 2) & 1, abort, lim);
       if (ok && !b2ok) ok = b2ok = warp_wait(bar(SB_B2FULL), 0, abort, lim);
-      if (ok && sl == 0 && j >= p.ND2) {
+      if (ok && sl == 0 && j >= p.ND2) {  // the D2 buffer's previous piece was read by C2
         ok = warp_wait(bar(SB_D2READ + ((j - p.ND2) & 1)), ((j - p.ND2) >> 1) & 1, abort, lim);
         tc_fence_after();
       }
@@ -303,13 +316,11 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
         if (sl == NSL - 1) commit_one(bar(SB_S2DONE + (j & 1)));
       }
     }
-    // Drain this warp's tensor-core work before the CTA barrier that precedes the TMEM release,
-    // whatever happened (another warp may raise the abort flag after the last MMA was issued).
-    commit_one(bar(SB_DRAIN));
-    if (lane == 0) mbar_drain_spin(bar(SB_DRAIN), 0);
+    commit_one(bar(SB_DRAIN + 1));  // drain this warp's tensor-core work (as the S1 issuer)
+    if (lane == 0) mbar_drain_spin(bar(SB_DRAIN + 1), 0);
     __syncwarp();
-  } else if (warp == 13) {
-    // ===================== issuer B: S3 of each piece =========================================
+  } else if (warp == 14) {
+    // ===================== S3 issuer: S3 of each piece ========================================
     pdl_wait();
     bool ok = true;
     const uint32_t sbo3 = (uint32_t)(p.K3P / 8) * 128;
@@ -333,13 +344,13 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
         if (j == np - 1) commit_one(bar(SB_D3DONE));
       }
     }
-    commit_one(bar(SB_DRAIN + 1));  // drain this warp's tensor-core work (as issuer A)
-    if (lane == 0) mbar_drain_spin(bar(SB_DRAIN + 1), 0);
+    commit_one(bar(SB_DRAIN + 2));  // drain this warp's tensor-core work (as the S1 issuer)
+    if (lane == 0) mbar_drain_spin(bar(SB_DRAIN + 2), 0);
     __syncwarp();
   } else {
     // ---- first x slices, staged by the converter and feeder warps
-    const int bt = tid < 384 ? tid : tid - 64;
-    if (np > 0 && warp == 14 && lane == 0) {  // the feeder's first bulk copies go out at once
+    const int bt = tid < 384 ? tid : tid - 96;
+    if (np > 0 && warp == 15 && lane == 0) {  // the feeder's first bulk copies go out at once
       bulk_load(b2s, p.b2 + (size_t)grp * p.b2_bytes, p.b2_bytes, bar(SB_B2FULL));
       if (p.b1_all) {
         bulk_load(g1s, p.b1, sh.R * NSL * p.b1_bytes, bar(SB_G1FULL));
@@ -372,7 +383,8 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
       const bool rvalid = tq < p.TT;
       const int h = (sh.O1 + 1) >> 1;
       const int o1a = (warp >> 2) ? h : 0, o1b = (warp >> 2) ? sh.O1 : h;
-      const int nld = ((o1b - o1a) * 8 + 15) >> 4;  // 16-column TMEM loads of this half
+      const int SW = p.SW;                            // D1 slab columns (o1, ul): o1 * SW + ul
+      const int nld = ((o1b - o1a) * SW + 15) >> 4;  // 16-column TMEM loads of this half
       constexpr int CB = 4;                          // loads in flight per wait
       bool ok = true;
       for (int g = 0; g < G; ++g) {
@@ -383,7 +395,7 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
         if (ok) {
           tc_fence_after();
           unsigned char* a2 = smem + p.off_a2 + (g % p.NA2) * p.a2_bytes;
-          const uint32_t d1 = tmem + lane_base + d1_col(g) + o1a * 8;
+          const uint32_t d1 = tmem + lane_base + d1_col(g) + o1a * SW;
           for (int cb = 0; cb < nld; cb += CB) {
             uint32_t v[CB][16];
 #pragma unroll
@@ -396,7 +408,7 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
               if (lane == 0) mbar_arrive(bar(SB_D1READ + (g & 1)));
               d1_read = true;
             }
-            if (rvalid) {
+            if (rvalid && SW == 8) {
 #pragma unroll
               for (int c = 0; c < CB; ++c) {
 #pragma unroll
@@ -409,6 +421,21 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
                   }
                 }
               }
+            } else if (rvalid) {  // SW 4: one load = four o1, half a chunk (8 bytes) each
+#pragma unroll
+              for (int c = 0; c < CB; ++c) {
+#pragma unroll
+                for (int hh = 0; hh < 4; ++hh) {
+                  const int o1 = o1a + 4 * (cb + c) + hh;
+                  if (cb + c < nld && o1 < o1b) {
+                    const int row = tq * sh.O1 + o1;
+                    const uint32_t* w = v[c] + 4 * hh;
+                    *reinterpret_cast<uint2*>(a2 + sl_a2_offset(row, i2 >> 1) + (i2 & 1) * 8) =
+                        make_uint2(pack2<__half>(__uint_as_float(w[0]), __uint_as_float(w[1])),
+                                   pack2<__half>(__uint_as_float(w[2]), __uint_as_float(w[3])));
+                  }
+                }
+              }
             }
           }
           fence_async_smem();
@@ -417,7 +444,7 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(SB_D1READ + (g & 1)));
         }
-        __syncwarp();  // hand slab g to issuer A
+        __syncwarp();  // hand slab g to the S2 issuer
         if (lane == 0) mbar_arrive(bar(SB_C1DONE + (g & 3)));
       }
     } else if (warp < 12) {
@@ -436,6 +463,8 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
           unsigned char* rowp = smem + p.off_a3 + ab * p.a3_bytes +
                                 (r >> 3) * ((p.K3P / 8) * 128) + (r & 7) * 16;
           constexpr int CB2 = 4;
+          // D2 column = o * RV + v, walked in 8-column chunks: (o, vv) advance without division
+          int o = 0, vv = 0;
           for (int c0 = 0; c0 < p.N2; c0 += 16 * CB2) {
             uint32_t v[CB2][16];
 #pragma unroll
@@ -451,11 +480,14 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
             for (int c = 0; c < CB2; ++c) {
 #pragma unroll
               for (int hh = 0; hh < 2; ++hh) {
-                const int col = c0 + c * 16 + 8 * hh;  // D2 column = o * RV + v
-                if (col < p.N2) {
-                  const int o = col / p.RV, vv = col - o * p.RV;
+                if (c0 + c * 16 + 8 * hh < p.N2) {
                   *reinterpret_cast<uint4*>(rowp + o * a3_block + (vv >> 3) * 128) =
                       sl_chunk_f16(v[c] + 8 * hh);
+                  vv += 8;
+                  if (vv == p.RV) {
+                    vv = 0;
+                    ++o;
+                  }
                 }
               }
             }
@@ -465,7 +497,7 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(SB_D2READ + db));
         }
-        __syncwarp();  // hand piece j to issuer B
+        __syncwarp();  // hand piece j to the S3 issuer
         if (lane == 0) mbar_arrive(bar(SB_C2DONE + (j & 1)));
       }
     } else {
@@ -773,6 +805,7 @@ static void fill_slab(SlabParams<S>& sp, const Plan& p, const SlabGeom& g, const
   sp.NC = g.NC;
   sp.NG = l.NG;
   sp.O2G = l.O2G;
+  sp.SW = l.SW;
   sp.NSL = l.NSL;
   sp.N1S = l.N1S;
   sp.KSS = l.KSL / 16;
@@ -806,7 +839,7 @@ static void fill_slab(SlabParams<S>& sp, const Plan& p, const SlabGeom& g, const
   sp.b3_all = g.b3_all;
   sp.ystr = g.ystr;
   sp.part_elems = (int)g.part_elems;
-  sp.zero_a2 = p.c.I2 * 8 < l.KSL;
+  sp.zero_a2 = p.c.I2 * l.SW < l.KSL;
   const Canon& c = p.c;
   sp.vec_out = c.sy3 == 1 && c.O3 % 8 == 0 && c.sy1 % 8 == 0 && c.sy2 % 8 == 0 &&
                c.d_out % 8 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;

@@ -12,14 +12,15 @@
 //   S3  D3[o2][(t,o1), o3] += A3[o2] . B3_piece[o3, v]                  (accumulated over pieces)
 // D1 and D2 live either in separate TMEM buffers (one or two D1, two D2) or, when that makes the
 // o2 groups wider, in two shared buffers that hold a piece's D1 and then its D2.
-// Roles (480 threads):
+// Roles (512 threads):
 //   warps 0-7   C1 (warps w and w+4 read the same TMEM lanes, each half of the o1 range)
 //   warps 8-11  C2, and the D3 read-out with warps 0-7 after the last piece
-//   warp 12     issuer A: S2 of each piece, and S1 of a later piece into the D1 buffer C1 just
-//               read (separate TMEM buffers)
-//   warp 13     issuer B: S3 of each piece, and S1 of the piece two later into the buffer that
-//               held D2 (shared buffers)
-//   warp 14     feeder: B2, B1, B3 by TMA bulk copy (all at once when they fit, else rings
+//   warp 12     S2 issuer: S2 of each piece
+//   warp 13     S3 issuer: S3 of each piece
+//   warp 14     S1 issuer: S1 of each piece into the D1 buffer its previous user released (C1
+//               read it; with shared buffers, C2 read the D2 it held); one issuing warp per
+//               stage, so a stage that waits holds up no other
+//   warp 15     feeder: B2, B1, B3 by TMA bulk copy (all at once when they fit, else rings
 //               refilled as the tensor-core stages release slots) and the x slice A1 of each
 //               further i3 (the first two are staged by the converter and feeder warps)
 // A converter group hands its work to the issuers through mbarriers (one arrival per warp): as
@@ -59,7 +60,7 @@ namespace cg = cooperative_groups;
 
 namespace trr {
 
-constexpr int kTcThreads = 480;
+constexpr int kTcThreads = 512;
 constexpr int kBuildThreads = 416;  // converter and feeder warps: first x slices
 constexpr int kBarBuild = 1;  // named barrier of the first x slices (0 is __syncthreads)
 constexpr unsigned kPollLimit = 1u << 24;    // loader polls without progress before it gives up
@@ -80,7 +81,8 @@ enum {
   BAR_C1DONE = 52,  // [2] C1 warps finished piece j (count 8), index j % 2
   BAR_C2DONE = 54,  // [2] C2 warps finished piece j (count 4), index j % 2
   BAR_D1READ = 56,  // [2] C1 warps read D1(j) (count 8), index j % 2
-  BAR_COUNT = 58
+  BAR_DRAIN3 = 58,  // after the piece loop: the S1 issuer's own work completed
+  BAR_COUNT = 59
 };
 
 template <class S>
@@ -273,25 +275,37 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   // access to x, y or the workspace.  Only the packed cores are read earlier, by the feeder's
   // first bulk copies: they are written by nothing but tr_pack_cores, which ends with a normally
   // serialized launch.
-  if (warp == 12) {
-    // ===================== issuer A: S2 of each piece (and S1, separate buffers) ==============
+  if (warp == 14) {
+    // ===================== S1 issuer: S1(k) once its D1 buffer was read ======================
+    // separate buffers: C1 read D1(k - ND1); shared buffers: C2 read D2(k - 2), the buffer's
+    // last use.  S1 runs ahead on its own, so C1 is fed whatever S2 and S3 wait for.
+    pdl_wait();
+    bool ok = true;
+    for (int k = 0; k < np && ok; ++k) {
+      if (!p.shared_d12 && k >= p.ND1)
+        ok = warp_wait(bar(BAR_D1READ + ((k - p.ND1) & 1)), ((k - p.ND1) >> 1) & 1, abort,
+                       p.spin_limit);
+      if (p.shared_d12 && k >= 2)
+        ok = warp_wait(bar(BAR_D2READ + (k & 1)), ((k - 2) >> 1) & 1, abort, p.spin_limit);
+      tc_fence_after();
+      if (ok) ok = issue_s1(k);
+    }
+    // Drain this warp's tensor-core work before the CTA barrier that precedes the TMEM release,
+    // whatever happened: another warp may raise the abort flag after this loop issued its last
+    // MMA, and then no one waits for D3DONE.
+    commit_one(bar(BAR_DRAIN3));
+    if (lane == 0) mbar_drain_spin(bar(BAR_DRAIN3), 0);
+    __syncwarp();
+  } else if (warp == 12) {
+    // ===================== S2 issuer: S2 of each piece ========================================
     // The whole warp runs the loop (uniform decisions); one elected lane issues.
     pdl_wait();
     bool ok = true, b2ok = false;
-    if (np > 0) {  // the first S1s: as many as there are D1 buffers
-      const int first = p.shared_d12 ? 2 : p.ND1;
-      for (int k = 0; k < first && k < np && ok; ++k) ok = issue_s1(k);
-    }
     const uint32_t sbo2 = (uint32_t)(sh.K2P / 8) * 128;
     const uint32_t idesc2 = umma_idesc<__half>(128, p.N2);
     for (int j = 0; j < np; ++j) {
       // No abort test in this loop: every wait checks the flag on its slow path, and an MMA
       // issued after a timeout only computes values the caller discards.
-      // ---- S1(j + ND1) into the D1 buffer C1 has just read (separate arrangement)
-      if (ok && !p.shared_d12 && j + p.ND1 < np) {
-        ok = warp_wait(bar(BAR_D1READ + (j & 1)), (j >> 1) & 1, abort, p.spin_limit);
-        if (ok) ok = issue_s1(j + p.ND1);
-      }
       // ---- S2(j): C1(j) wrote A2(j); the D2 buffer's previous piece was read by C2
       if (ok) ok = warp_wait(bar(BAR_C1DONE + (j & 1)), (j >> 1) & 1, abort, p.spin_limit);
       if (ok && !b2ok) ok = b2ok = warp_wait(bar(BAR_B2FULL), 0, abort, p.spin_limit);
@@ -305,24 +319,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
         commit_one(bar(BAR_S2DONE + (j & 1)));
       }
     }
-    // Drain this warp's tensor-core work before the CTA barrier that precedes the TMEM release,
-    // whatever happened: another warp may raise the abort flag after this loop issued its last
-    // MMA, and then no one waits for D3DONE.
-    commit_one(bar(BAR_DRAIN));
+    commit_one(bar(BAR_DRAIN));  // drain this warp's tensor-core work (as the S1 issuer)
     if (lane == 0) mbar_drain_spin(bar(BAR_DRAIN), 0);
     __syncwarp();
   } else if (warp == 13) {
-    // ===================== issuer B: S3 of each piece (and S1, shared buffers) ================
+    // ===================== S3 issuer: S3 of each piece ========================================
     pdl_wait();
     bool ok = true;
     const uint32_t sbo3 = (uint32_t)(K3 / 8) * 128;
     const uint32_t idesc3 = umma_idesc<__half>(128, p.N3P);
     for (int j = 0; j < np; ++j) {
-      // ---- S1(j + 2) into the buffer whose D2(j) C2 has just read (shared arrangement)
-      if (ok && p.shared_d12 && j + 2 < np) {
-        ok = warp_wait(bar(BAR_D2READ + (j & 1)), (j >> 1) & 1, abort, p.spin_limit);
-        if (ok) ok = issue_s1(j + 2);
-      }
       // ---- S3(j): C2(j) wrote A3(j); B3 landed
       if (ok) ok = warp_wait(bar(BAR_C2DONE + (j & 1)), (j >> 1) & 1, abort, p.spin_limit);
       if (ok)
@@ -338,13 +344,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
         if (j == np - 1) commit_one(bar(BAR_D3DONE));
       }
     }
-    commit_one(bar(BAR_DRAIN + 1));  // drain this warp's tensor-core work (as issuer A)
+    commit_one(bar(BAR_DRAIN + 1));  // drain this warp's tensor-core work (as the S1 issuer)
     if (lane == 0) mbar_drain_spin(bar(BAR_DRAIN + 1), 0);
     __syncwarp();
   } else {
     // ---- first x slices, staged by the converter and feeder warps
-    const int bt = tid < 384 ? tid : tid - 64;
-    if (np > 0 && warp == 14 && lane == 0) {  // the feeder's first bulk copies go out at once
+    const int bt = tid < 384 ? tid : tid - 96;
+    if (np > 0 && warp == 15 && lane == 0) {  // the feeder's first bulk copies go out at once
       bulk_load(b2s, p.b2 + (size_t)grp * p.b2_bytes, p.b2_bytes, bar(BAR_B2FULL));
       if (p.b1_all) {
         bulk_load(g1s, p.b1, sh.R * p.b1_bytes, bar(BAR_G1FULL));
@@ -433,7 +439,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(BAR_D1READ + (j & 1)));
         }
-        __syncwarp();  // hand piece j to issuer A
+        __syncwarp();  // hand piece j to the S2 issuer
         if (lane == 0) mbar_arrive(bar(BAR_C1DONE + (j & 1)));
       }
     } else if (warp < 12) {
@@ -480,7 +486,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(BAR_D2READ + db));
         }
-        __syncwarp();  // hand piece j to issuer B
+        __syncwarp();  // hand piece j to the S3 issuer
         if (lane == 0) mbar_arrive(bar(BAR_C2DONE + (j & 1)));
       }
     } else {

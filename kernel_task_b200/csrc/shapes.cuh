@@ -59,13 +59,16 @@ struct FixedShape {
 // The compiled benchmark shapes (order = the planner's cheapest ring order):
 //   c1/c2  1920->2880 (8,12,20)->(12,10,24), R 8 / 16, order B,A,C
 //   c4     4096-hidden decode-chain layers at R 16: q/o, k/v, gate/up (order A,B,C), down (C,B,A)
+//   c1 down  2880->1920 (12,10,24)->(8,12,20), R 8, order C,A,B: the down layer of the
+//            1920 -> 2880 -> 1920 chain (the reference's multi-layer comparison point)
 #define TRR_FIXED_SHAPES(X)                  \
   X(8, 12, 20, 12, 10, 24, 8, 1, 0)          \
   X(8, 12, 20, 12, 10, 24, 16, 1, 0)         \
   X(16, 16, 16, 16, 16, 16, 16, 0, 1)        \
   X(16, 16, 16, 8, 8, 16, 16, 0, 1)          \
   X(16, 16, 16, 16, 28, 32, 16, 0, 1)        \
-  X(16, 28, 32, 16, 16, 16, 16, 2, 1)
+  X(16, 28, 32, 16, 16, 16, 16, 2, 1)        \
+  X(12, 10, 24, 8, 12, 20, 8, 2, 0)
 
 // The slab kernel also compiles the config-3 shape (rank 32, which the other tcgen05 kernel does
 // not take).

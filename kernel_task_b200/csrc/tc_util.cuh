@@ -106,6 +106,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, volati
 
 // Spinning bounded wait of one thread (test_wait polls; the abort flag is checked every 256).
 // `limit` polls without completion make the wait give up and raise the CTA's abort flag.
+#ifndef TRR_SPIN_BACKOFF_NS
+#define TRR_SPIN_BACKOFF_NS 0
+#endif
+#ifndef TRR_SPIN_TRYWAIT
+#define TRR_SPIN_TRYWAIT 1000
+#endif
 __device__ __forceinline__ bool mbar_spin(uint32_t mbar, uint32_t parity, volatile int* abort,
                                           unsigned limit = kSpinLimit) {
   for (unsigned i = 0; !mbar_test(mbar, parity); ++i) {
@@ -114,6 +120,21 @@ __device__ __forceinline__ bool mbar_spin(uint32_t mbar, uint32_t parity, volati
       *abort = 1;
       return false;
     }
+#if TRR_SPIN_TRYWAIT
+    if (i >= 4) {
+      uint32_t done;
+      asm volatile(
+          "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+          "selp.u32 %0, 1, 0, p;\n\t}\n"
+          : "=r"(done)
+          : "r"(mbar), "r"(parity), "r"(TRR_SPIN_TRYWAIT)
+          : "memory");
+      if (done) return true;
+    }
+#endif
+#if TRR_SPIN_BACKOFF_NS
+    if (i >= 4) __nanosleep(TRR_SPIN_BACKOFF_NS);
+#endif
   }
   return true;
 }

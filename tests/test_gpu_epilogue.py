@@ -28,14 +28,16 @@ DEV = "cuda"
 BF16_ULP2 = 2.0 ** -7  # two bf16 ulps, relative
 
 # (layer, tokens, kernel, tokens_per_tile, cluster, clusters): the decode kernel (T*O1 <= 16),
-# the tcgen05 kernel with one and several clusters per tile (workspace-slot reduction), and
-# the mma.sync kernel with a cross-cluster reduction
+# the tcgen05 and slab kernels with one and several clusters per tile (workspace-slot
+# reduction), and the mma.sync kernel with a cross-cluster reduction
 CASES = [
     ("q", 1, abi.KERNEL_DECODE, 1, 0, 0), ("gate", 1, abi.KERNEL_DECODE, 1, 0, 0),
     ("down", 1, abi.KERNEL_DECODE, 1, 0, 0), ("k", 2, abi.KERNEL_DECODE, 1, 16, 3),
     ("q", 8, abi.KERNEL_TC05, 0, 0, 0), ("gate", 24, abi.KERNEL_TC05, 0, 0, 0),
     ("down", 9, abi.KERNEL_TC05, 0, 2, 3), ("k", 33, abi.KERNEL_TC05, 0, 0, 0),
     ("q", 5, abi.KERNEL_MMA, 0, 0, 0), ("up", 3, abi.KERNEL_MMA, 1, 4, 5),
+    ("q", 8, abi.KERNEL_SLAB, 0, 0, 0), ("down", 9, abi.KERNEL_SLAB, 0, 2, 3),
+    ("gate", 40, abi.KERNEL_SLAB, 0, 0, 0),
 ]
 
 
@@ -55,7 +57,8 @@ def test_epilogues_match_unfused(case):
     name, T, kernel, TT, CL, NC = case
     s, cores, op = _layer(name)
     x = kspec.baseline_x(s, T, seed=T, dtype=torch.bfloat16, device=DEV)
-    assert op.tiling(T)["kernel"] in (abi.KERNEL_DECODE, abi.KERNEL_TC05, abi.KERNEL_MMA)
+    assert op.tiling(T)["kernel"] in (abi.KERNEL_DECODE, abi.KERNEL_TC05, abi.KERNEL_MMA,
+                                      abi.KERNEL_SLAB)
     run = lambda kind, aux=None, f32=False: op.call_epilogue(x, kind, aux, f32, kernel, TT, CL,
                                                              NC)
     y16 = run(abi.TR_EPI_NONE)

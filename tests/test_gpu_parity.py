@@ -378,3 +378,22 @@ def test_sharded_ring_single_process_matches_operator():
     ref = oracle.tr_forward_reference(x[rows].float().cpu().numpy(),
                                       [c.float().cpu().numpy() for c in cores])
     check_close(y[rows], ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("T", [1, 2, 8, 32])
+def test_c1_chain_down_layer(T):
+    """The down layer of the 1920 -> 2880 -> 1920 chain (2880 -> 1920, (12,10,24)->(8,12,20),
+    R8, order C,A,B; compiled as a fixed shape) on the kernel the planner picks, against the
+    oracle, and the decode kernel's one-wave cluster split."""
+    s = kspec.TRSpec((12, 10, 24), (8, 12, 20), 8)
+    cores = kspec.baseline_cores(s, seed=11, dtype=torch.float16, device=DEV)
+    fn = prepare_optimized(cores, s)
+    x = kspec.baseline_x(s, T, seed=11, dtype=torch.float16, device=DEV)
+    y = fn(x)
+    check_close(y, oracle.tr_forward_reference(x.float().cpu().numpy(),
+                                               [c.float().cpu().numpy() for c in cores]),
+                torch.float16)
+    torch.testing.assert_close(fn(x), y, rtol=0, atol=0)
+    if T == 1:
+        g = fn.tiling(1)
+        assert g["kernel"] == abi.KERNEL_DECODE and g["cluster"] <= 8

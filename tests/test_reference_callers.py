@@ -105,7 +105,9 @@ def test_reference_harness_case_through_the_patch(patched_tree, tmp_path):
     """One case of the reference's harness (benchmarks/benchmark.py: isolated child process per
     method, FP32 dense oracle after timing) with factorized_optimized = this library."""
     out = tmp_path / "results.json"
-    r = subprocess.run([sys.executable, "benchmarks/benchmark.py", "--device", "cuda",
+    # "cuda:0", not "cuda": the harness passes the device to torch.cuda.set_device, which on the
+    # torch of this image (2.11; the reference pins 2.14) needs an index
+    r = subprocess.run([sys.executable, "benchmarks/benchmark.py", "--device", "cuda:0",
                         "--dtype", "float16", "--rank", "8", "--tokens", "8", "--warmup", "5",
                         "--iterations", "10", "--event-block", "5", "--output", str(out)],
                        cwd=patched_tree, env=_env(patched_tree), capture_output=True, text=True,

@@ -116,6 +116,12 @@ def peaks():
     return 6650.0, 1590.0, 1400.0, "fallback"
 
 
+def clock_index(local_rank: int) -> int:
+    """nvidia-smi's index of this process's GPU (CUDA_VISIBLE_DEVICES renumbers torch's)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    return int(vis.split(",")[local_rank]) if vis else local_rank
+
+
 class Clocks:
     """nvidia-smi sampling during the timed region."""
 
@@ -152,7 +158,7 @@ class Clocks:
             self.proc.kill()
         self.file.flush()
         self.file.seek(0)
-        sm, smax, reasons = [], [], set()
+        sm, smax, watts, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.file.read().splitlines():
             f = [v.strip() for v in line.split(",")]
@@ -163,13 +169,17 @@ class Clocks:
                 smax.append(float(f[2].split()[0]))
             except ValueError:
                 continue
+            try:
+                watts.append(float(f[3].split()[0]))
+            except ValueError:
+                pass
             for n, v in zip(names, f[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
         os.unlink(self.file.name)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "power_w": statistics.median(watts) if watts else None}
 
 
 def dense_weight(cores):
@@ -528,6 +538,10 @@ def prefill_leg(args, rank, world, dev, tc_peak, tc_sustained):
         torch.distributed.barrier()
     steps = max(1, min(args.steps, 3))
     times = []
+    # clocks and power of this leg alone: a seconds-long tensor-core load, where a slower box
+    # (power cap, temperature) shows in the SM clock
+    clocks = Clocks(clock_index(dev.index if dev.index is not None else 0))
+    clocks.wait_first_sample()
     for _ in range(steps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -535,6 +549,7 @@ def prefill_leg(args, rank, world, dev, tc_peak, tc_sustained):
         e1.record()
         e1.synchronize()
         times.append(e0.elapsed_time(e1))
+    clk = clocks.stop()
     ms = max_over_ranks([statistics.mean(times)], world)[0]
     out = {"workload": "c5: 4096->14336 (16,16,16)->(16,28,32) R16 bf16, tokens split by rows, "
                        "cores replicated per GPU",
@@ -542,7 +557,7 @@ def prefill_leg(args, rank, world, dev, tc_peak, tc_sustained):
            "ms": round(ms, 3), "tokens_per_s": round(T / (ms * 1e-3), 1),
            "steps": steps, "scaling": "strong", "timing": "CUDA events, max over ranks",
            "kernel": KERNEL_NAMES.get(op.fn.tiling(b - a)["kernel"], "?"),
-           "tiling": op.fn.tiling(b - a)}
+           "tiling": op.fn.tiling(b - a), "clocks": clk}
     flops = op.fn.flops_per_token() * shard_bounds(T, world, 0)[1]
     tf = flops / (ms * 1e-3) / 1e12
     out["tflops_per_gpu"] = round(tf, 2)
@@ -781,8 +796,7 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    clocks = Clocks(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ
-                    else int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank]))
+    clocks = Clocks(clock_index(local_rank))
     clocks.wait_first_sample()
     launches = 0
     for key, c in cases.items():

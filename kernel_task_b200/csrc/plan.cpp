@@ -682,36 +682,45 @@ int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* f, TcGeom* g) {
   return TR_OK;
 }
 
-// Split of the slab kernel's pieces for `cols` tile columns, as tc_split: among the splits whose
-// cols * NC clusters of CL CTAs are co-resident (one wave), the least estimated time: the
-// longest CTA's pieces at about 0.3 us per rank slab, 1 us per extra x slice, and with NC > 1
-// the slot pass (2 us plus the slot traffic, NC / CL of a tile's partial sums at 1.4 us per
-// 69 KB).  With a column per SM or more, one CTA per column.
+// Split of the slab kernel's pieces for `cols` tile columns: CL CTAs per cluster and NC <= 5
+// clusters per column, by an estimate of the device time in microseconds:
+//   waves x pieces per CTA x (NSL slab steps of about 1 us + 0.3 us), where a wave holds
+//   max_clusters[CL] clusters (clusters of 8 fill 120 SMs of 148, of 4 132, of 2 all), plus with
+//   NC > 1 the slot pass (2 us plus NC / CL of a tile's partial sums at 1.4 us per 69 KB) and
+//   1 us per extra x slice of a CTA.
+// Fitted to forced splits of config 3 (R32) at T = 1, 2 and 128 (160 columns: one CTA per column
+// runs two waves, 4.25 ms; clusters of 4 or 2 x 2 slots, 2.7 ms).
 static void slab_split(const Plan& p, long long cols, int64_t rows, int* CL, int* NC) {
   const Canon& c = p.c;
   const MmaLayout& m = p.m;
   const SlabLayout& l = p.sl;
+  const double piece_us = 1.0 * l.NSL + 0.3;
+  const double part_kb = (double)rows * l.O2G * c.O3 * 4 / 1024.0;
+  // the slot pass is real traffic once the columns alone fill the device: at most 2 slots then
+  const int nc_cap = cols >= p.num_sms ? 2 : 5;
+  double best = 1e30, whole = 0.0;
   *CL = 1;
   *NC = 1;
-  if (cols >= p.num_sms) return;
-  const double piece_us = 0.3 * l.NSL;
-  const double part_kb = (double)rows * l.O2G * c.O3 * 4 / 1024.0;
-  double best = 1e30;
   for (int cl = 16; cl >= 1; cl /= 2) {
-    if (cl > m.npieces || cols > p.max_clusters[cl]) continue;
-    const long long nc_max =
-        std::min<long long>(std::min<long long>(p.max_clusters[cl] / cols, m.npieces / cl), 5);
+    if (cl > m.npieces || p.max_clusters[cl] < 1) continue;
+    const int nc_max = std::min(nc_cap, m.npieces / cl);
     for (int nc = 1; nc <= nc_max; ++nc) {
       const int NJ = cl * nc;
-      double est = piece_us * ceil_div(m.npieces, NJ) +
+      const long long waves = (cols * nc + p.max_clusters[cl] - 1) / p.max_clusters[cl];
+      double est = (double)waves * ceil_div(m.npieces, NJ) * piece_us +
                    1.0 * (max_i3_span(m.npieces, c.R, NJ) - 1);
       if (nc > 1) est += 2.0 + 1.4 * ((double)nc / cl) * part_kb / 67.5;
+      if (NJ == 1) whole = est;
       if (est < best - 1e-9) {
         best = est;
         *CL = cl;
         *NC = nc;
       }
     }
+  }
+  if (whole > 0.0 && whole <= 1.1 * best) {  // a split must gain at least 10%
+    *CL = 1;
+    *NC = 1;
   }
 }
 

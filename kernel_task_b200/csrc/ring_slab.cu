@@ -65,7 +65,6 @@ namespace trr {
 
 constexpr int kSlThreads = 512;
 constexpr int kSlBuildThreads = 416;  // converter and feeder warps: first x slices
-constexpr int kSlBarBuild = 1;        // named barrier of the first x slices (0 is __syncthreads)
 constexpr unsigned kSlPollLimit = 1u << 24;  // feeder polls without progress before it gives up
 constexpr int kSwSlab = 128 * 128;           // bytes of one 64-wide K slab of an A2 slot
 
@@ -196,7 +195,18 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
   // packed B1 slice of slab step r: (s, sl) of piece r / NSL
   auto b1_slice = [&](int r) { return ((pa + r / NSL) % sh.R) * NSL + r % NSL; };
 
-  // ---- TMEM, mbarriers, zeroed pads of the A operands (never-written K columns)
+  const uint32_t a1s = smem_u32(smem + p.off_a1);
+  const uint32_t g1s = smem_u32(smem + p.off_g1);
+  const uint32_t a2s = smem_u32(smem + p.off_a2);
+  const uint32_t b2s = smem_u32(smem + p.off_b2);
+  const uint32_t a3s = smem_u32(smem + p.off_a3);
+  const uint32_t b3s = smem_u32(smem + p.off_b3);
+
+  // ---- set-up, all before one CTA barrier: warp 0 allocates TMEM; the feeder warp initialises
+  // the mbarriers (one per lane: one thread initialising them all took 2 us) and sends its first
+  // bulk copies of packed cores; every thread zeroes its share of the A-operand pads
+  // (never-written K columns); the converter and feeder warps stage the first x slices after
+  // griddepcontrol.wait, so the x gather overlaps the set-up.
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
                      smem_u32(tmem_slot)),
@@ -204,8 +214,8 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
   }
-  if (tid == 32) {
-    for (int i = 0; i < SB_COUNT; ++i) {
+  if (warp == 15) {
+    for (int i = lane; i < SB_COUNT; i += 32) {
       int count = 1;
       if ((i >= SB_D1READ && i < SB_D1READ + 2) || (i >= SB_C1DONE && i < SB_C1DONE + 4))
         count = 8;
@@ -214,9 +224,32 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar(i)), "r"(count)
                    : "memory");
     }
+    // each lane's initialised barriers, visible to the async proxy before the first complete_tx
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-    *flag = 0;
-    *abort = 0;
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      *flag = 0;
+      *abort = 0;
+      if (np > 0) {  // the feeder's first bulk copies go out at once
+        bulk_load(b2s, p.b2 + (size_t)grp * p.b2_bytes, p.b2_bytes, bar(SB_B2FULL));
+        if (p.b1_all) {
+          bulk_load(g1s, p.b1, sh.R * NSL * p.b1_bytes, bar(SB_G1FULL));
+        } else {
+          for (int r = 0; r < p.NB1 && r < G; ++r)
+            bulk_load(g1s + r * p.b1_bytes, p.b1 + (size_t)b1_slice(r) * p.b1_bytes,
+                      p.b1_bytes, bar(SB_G1FULL + r));
+        }
+        if (p.b3_all) {
+          bulk_load(b3s, p.b3 + (size_t)pa * p.b3_bytes, np * p.b3_bytes, bar(SB_B3FULL));
+        } else {
+          for (int q = 0; q < p.NB3 && q < np; ++q)
+            bulk_load(b3s + q * p.b3_bytes, p.b3 + (size_t)(pa + q) * p.b3_bytes, p.b3_bytes,
+                      bar(SB_B3FULL + q));
+        }
+      }
+    }
+    __syncwarp();
   }
   if (p.zero_a2) {
     uint4* z = reinterpret_cast<uint4*>(smem + p.off_a2);
@@ -228,19 +261,20 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
     const int n16 = p.NA3 * p.a3_bytes / 16;
     for (int i = tid; i < n16; i += kSlThreads) z[i] = make_uint4(0u, 0u, 0u, 0u);
   }
+  if (warp < 12 || warp == 15) {  // first x slices: converter and feeder warps
+    const int bt = tid < 384 ? tid : tid - 96;
+    pdl_wait();
+    for (int q = 0; q < 2 && q < nq; ++q)
+      sl_build_a1(sh, smem + p.off_a1 + q * p.a1_bytes, xt, TTv, i3a + q, bt, kSlBuildThreads);
+  }
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (tid == 0)
+    for (int q = 0; q < 2 && q < nq; ++q) mbar_arrive(bar(SB_A1FULL + q));
   const uint32_t tmem = *tmem_slot;
   const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-
-  const uint32_t a1s = smem_u32(smem + p.off_a1);
-  const uint32_t g1s = smem_u32(smem + p.off_g1);
-  const uint32_t a2s = smem_u32(smem + p.off_a2);
-  const uint32_t b2s = smem_u32(smem + p.off_b2);
-  const uint32_t a3s = smem_u32(smem + p.off_a3);
-  const uint32_t b3s = smem_u32(smem + p.off_b3);
 
   // S1 of slab step g, issued by a converged warp: waits for its x slice and B1 slab slice
   // (each only once when it does not change), accumulates into D1 slab buffer g & 1, signals
@@ -348,34 +382,6 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
     if (lane == 0) mbar_drain_spin(bar(SB_DRAIN + 2), 0);
     __syncwarp();
   } else {
-    // ---- first x slices, staged by the converter and feeder warps
-    const int bt = tid < 384 ? tid : tid - 96;
-    if (np > 0 && warp == 15 && lane == 0) {  // the feeder's first bulk copies go out at once
-      bulk_load(b2s, p.b2 + (size_t)grp * p.b2_bytes, p.b2_bytes, bar(SB_B2FULL));
-      if (p.b1_all) {
-        bulk_load(g1s, p.b1, sh.R * NSL * p.b1_bytes, bar(SB_G1FULL));
-      } else {
-        for (int r = 0; r < p.NB1 && r < G; ++r)
-          bulk_load(g1s + r * p.b1_bytes, p.b1 + (size_t)b1_slice(r) * p.b1_bytes, p.b1_bytes,
-                    bar(SB_G1FULL + r));
-      }
-      if (p.b3_all) {
-        bulk_load(b3s, p.b3 + (size_t)pa * p.b3_bytes, np * p.b3_bytes, bar(SB_B3FULL));
-      } else {
-        for (int q = 0; q < p.NB3 && q < np; ++q)
-          bulk_load(b3s + q * p.b3_bytes, p.b3 + (size_t)(pa + q) * p.b3_bytes, p.b3_bytes,
-                    bar(SB_B3FULL + q));
-      }
-    }
-    __syncwarp();
-    pdl_wait();
-    for (int q = 0; q < 2 && q < nq; ++q)
-      sl_build_a1(sh, smem + p.off_a1 + q * p.a1_bytes, xt, TTv, i3a + q, bt, kSlBuildThreads);
-    fence_async_smem();
-    named_sync(kSlBarBuild, kSlBuildThreads);
-    if (tid == 0)
-      for (int q = 0; q < 2 && q < nq; ++q) mbar_arrive(bar(SB_A1FULL + q));
-
     if (warp < 8) {
       // ============================ C1: D1 slab -> A2 slot ======================================
       const int r1 = 32 * (warp & 3) + lane;  // D1 row (t, i2)

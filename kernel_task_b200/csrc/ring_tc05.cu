@@ -62,7 +62,6 @@ namespace trr {
 
 constexpr int kTcThreads = 512;
 constexpr int kBuildThreads = 416;  // converter and feeder warps: first x slices
-constexpr int kBarBuild = 1;  // named barrier of the first x slices (0 is __syncthreads)
 constexpr unsigned kPollLimit = 1u << 24;    // loader polls without progress before it gives up
 constexpr int kA2Slab = 128 * 128;  // bytes of one 64-wide K slab of A2
 
@@ -193,7 +192,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   auto d1_col = [&](int j) { return p.shared_d12 ? (j & 1) * p.DBW : (j % p.ND1) * p.N1P; };
   auto d2_col = [&](int j) { return p.shared_d12 ? (j & 1) * p.DBW : p.d2_col + (j & 1) * p.N2; };
 
-  // ---- TMEM, mbarriers, zeroed pads of the A operands (never-written rows/columns)
+  const uint32_t a1s = smem_u32(smem + p.off_a1);
+  const uint32_t g1s = smem_u32(smem + p.off_g1);
+  const uint32_t a2s = smem_u32(smem + p.off_a2);
+  const uint32_t b2s = smem_u32(smem + p.off_b2);
+  const uint32_t a3s = smem_u32(smem + p.off_a3);
+  const uint32_t b3s = smem_u32(smem + p.off_b3);
+  const int NB1 = p.NB1;
+
+  // ---- set-up, all before one CTA barrier: warp 0 allocates TMEM; the feeder warp initialises
+  // the mbarriers (one per lane: one thread initialising them all took 2 us, the longest part
+  // of the set-up) and sends its first bulk copies of packed cores; every thread zeroes its
+  // share of the A-operand pads (never-written rows/columns); the converter and feeder warps
+  // stage the first x slices after griddepcontrol.wait, so the x gather overlaps the set-up.
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
                      smem_u32(tmem_slot)),
@@ -201,8 +212,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
   }
-  if (tid == 32) {
-    for (int i = 0; i < BAR_COUNT; ++i) {
+  if (warp == 15) {
+    for (int i = lane; i < BAR_COUNT; i += 32) {
       int count = 1;
       if ((i >= BAR_D2READ && i < BAR_D2READ + 2) || (i >= BAR_C2DONE && i < BAR_C2DONE + 2))
         count = 4;
@@ -211,9 +222,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar(i)), "r"(count)
                    : "memory");
     }
+    // each lane's initialised barriers, visible to the async proxy before the first complete_tx
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-    *flag = 0;
-    *abort = 0;
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      *flag = 0;
+      *abort = 0;
+      if (np > 0) {  // the feeder's first bulk copies go out at once
+        bulk_load(b2s, p.b2 + (size_t)grp * p.b2_bytes, p.b2_bytes, bar(BAR_B2FULL));
+        if (p.b1_all) {
+          bulk_load(g1s, p.b1, sh.R * p.b1_bytes, bar(BAR_G1FULL));
+        } else {
+          for (int q = 0; q < NB1 && q < np; ++q)
+            bulk_load(g1s + q * p.b1_bytes, p.b1 + (size_t)((pa + q) % sh.R) * p.b1_bytes,
+                      p.b1_bytes, bar(BAR_G1FULL + q));
+        }
+        if (p.b3_all) {
+          bulk_load(b3s, p.b3 + (size_t)pa * p.b3_bytes, np * p.b3_bytes, bar(BAR_B3FULL));
+        } else {
+          for (int q = 0; q < p.NB3 && q < np; ++q)
+            bulk_load(b3s + q * p.b3_bytes, p.b3 + (size_t)(pa + q) * p.b3_bytes, p.b3_bytes,
+                      bar(BAR_B3FULL + q));
+        }
+      }
+    }
+    __syncwarp();
   }
   if (p.TT * sh.O1 < 128 || sh.I2 * RP < sh.K2P) {
     uint4* z = reinterpret_cast<uint4*>(smem + p.off_a2);
@@ -225,20 +259,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
     const int n16 = p.NA3 * p.a3_bytes / 16;
     for (int i = tid; i < n16; i += kTcThreads) z[i] = make_uint4(0u, 0u, 0u, 0u);
   }
+  if (warp < 12 || warp == 15) {  // first x slices: converter and feeder warps
+    const int bt = tid < 384 ? tid : tid - 96;
+    pdl_wait();
+    for (int q = 0; q < 2 && q < nq; ++q)
+      build_a1(sh, smem + p.off_a1 + q * p.a1_bytes, xt, TTv, i3a + q, bt, kBuildThreads);
+  }
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (tid == 0)
+    for (int q = 0; q < 2 && q < nq; ++q) mbar_arrive(bar(BAR_A1FULL + q));
   const uint32_t tmem = *tmem_slot;
   const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-
-  const uint32_t a1s = smem_u32(smem + p.off_a1);
-  const uint32_t g1s = smem_u32(smem + p.off_g1);
-  const uint32_t a2s = smem_u32(smem + p.off_a2);
-  const uint32_t b2s = smem_u32(smem + p.off_b2);
-  const uint32_t a3s = smem_u32(smem + p.off_a3);
-  const uint32_t b3s = smem_u32(smem + p.off_b3);
-  const int NB1 = p.NB1;
 
   // S1(k), issued by a converged warp: waits for its x slice and B1 (each only once when it
   // does not change from piece to piece), accumulates into D1(k), signals S1DONE (and A1FREE
@@ -348,34 +382,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
     if (lane == 0) mbar_drain_spin(bar(BAR_DRAIN + 1), 0);
     __syncwarp();
   } else {
-    // ---- first x slices, staged by the converter and feeder warps
-    const int bt = tid < 384 ? tid : tid - 96;
-    if (np > 0 && warp == 15 && lane == 0) {  // the feeder's first bulk copies go out at once
-      bulk_load(b2s, p.b2 + (size_t)grp * p.b2_bytes, p.b2_bytes, bar(BAR_B2FULL));
-      if (p.b1_all) {
-        bulk_load(g1s, p.b1, sh.R * p.b1_bytes, bar(BAR_G1FULL));
-      } else {
-        for (int q = 0; q < NB1 && q < np; ++q)
-          bulk_load(g1s + q * p.b1_bytes, p.b1 + (size_t)((pa + q) % sh.R) * p.b1_bytes,
-                    p.b1_bytes, bar(BAR_G1FULL + q));
-      }
-      if (p.b3_all) {
-        bulk_load(b3s, p.b3 + (size_t)pa * p.b3_bytes, np * p.b3_bytes, bar(BAR_B3FULL));
-      } else {
-        for (int q = 0; q < p.NB3 && q < np; ++q)
-          bulk_load(b3s + q * p.b3_bytes, p.b3 + (size_t)(pa + q) * p.b3_bytes, p.b3_bytes,
-                    bar(BAR_B3FULL + q));
-      }
-    }
-    __syncwarp();
-    pdl_wait();
-    for (int q = 0; q < 2 && q < nq; ++q)
-      build_a1(sh, smem + p.off_a1 + q * p.a1_bytes, xt, TTv, i3a + q, bt, kBuildThreads);
-    fence_async_smem();
-    named_sync(kBarBuild, kBuildThreads);
-    if (tid == 0)
-      for (int q = 0; q < 2 && q < nq; ++q) mbar_arrive(bar(BAR_A1FULL + q));
-
     if (warp < 8) {
       // ============================ C1: D1 -> A2 ============================
       const int r1 = 32 * (warp & 3) + lane;  // D1 row (t, i2)

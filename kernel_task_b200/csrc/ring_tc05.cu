@@ -100,7 +100,7 @@ struct TcParams {
   int b1_bytes, b2_bytes, b3_bytes;
   int off_a2, off_b2, off_a3, off_a1, off_g1, off_b3, off_bar;
   int NA2, NA3, NB1, b1_all, NB3, b3_all, a2_bytes, a3_bytes, a1_bytes;
-  int ystr, vec_out, slot_elems;
+  int ystr, vec_out, vec_out4, slot_elems;
   float* parts;    // per-CTA partial sums in the workspace (CL > 1)
   int part_elems;  // floats of one CTA's partial sums
   unsigned spin_limit;  // polls of one bounded wait before it gives up (tr_plan_set_wait_limit)
@@ -559,11 +559,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   }
 
   pdl_trigger();  // the next kernel may set up while this one reduces
-  // ---- D3 -> partial y of this CTA (rows (t,o1), columns (o of group, o3)), fp32 in smem.
-  // D3DONE: every tensor-core operation completed, so the operand space is free.
+  // ---- D3 -> partial y of this CTA (rows (t,o1), columns (o of group, o3)).
+  // Cluster of CTAs with O3 a multiple of 4 (lm): straight from the TMEM loads to this CTA's
+  // workspace area in L2, lane-major (float4 of column quad q = (o, o3 / 4) of row r at
+  // q * RS + r), so that the stores need no staging and every warp store covers 512 contiguous
+  // bytes.  Otherwise into shared memory (rows of ystr floats; the operand space is free once
+  // D3DONE has completed every tensor-core operation).
   __syncthreads();
   float* ys = reinterpret_cast<float*>(smem);
   const int ystr = p.ystr;
+  const bool lm = p.CL > 1 && (sh.O3 & 3) == 0;
+  const int RS = p.TT * sh.O1;  // rows of a tile: the row stride of the lane-major layout
+  float4* mine4 = reinterpret_cast<float4*>(p.parts + (size_t)blockIdx.x * p.part_elems);
   if (warp < 12) {
     const bool ok = np > 0 && mbar_spin(bar(BAR_D3DONE), 0, abort, p.spin_limit);
     tc_fence_after();
@@ -592,16 +599,35 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
 #pragma unroll
           for (int i = 0; i < 16; ++i) w[i] = 0u;
         }
-        if (r < rows)
-          for (int i = 0; i < 16; ++i)
-            if (c16 * 16 + i < sh.O3) ys[r * ystr + o * sh.O3 + c16 * 16 + i] = __uint_as_float(w[i]);
+        if (r < rows) {
+          if (lm) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (c16 * 16 + 4 * k < sh.O3)
+                __stcg(mine4 + (size_t)(o * (sh.O3 >> 2) + c16 * 4 + k) * RS + r,
+                       make_float4(__uint_as_float(w[4 * k]), __uint_as_float(w[4 * k + 1]),
+                                   __uint_as_float(w[4 * k + 2]), __uint_as_float(w[4 * k + 3])));
+          } else {
+            for (int i = 0; i < 16; ++i)
+              if (c16 * 16 + i < sh.O3)
+                ys[r * ystr + o * sh.O3 + c16 * 16 + i] = __uint_as_float(w[i]);
+          }
+        }
       }
       if (r < rows) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           if (c >= nc16) break;
           float* dst = ys + r * ystr + o * sh.O3 + c * 16;
-          if (vec4) {
+          if (lm) {  // column quads (o, o3 / 4) of this row, lane-major: a warp store is 512 B
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (c * 16 + 4 * k < sh.O3)
+                __stcg(mine4 + (size_t)(o * (sh.O3 >> 2) + c * 4 + k) * RS + r,
+                       make_float4(__uint_as_float(v[c][4 * k]), __uint_as_float(v[c][4 * k + 1]),
+                                   __uint_as_float(v[c][4 * k + 2]),
+                                   __uint_as_float(v[c][4 * k + 3])));
+          } else if (vec4) {
 #pragma unroll
             for (int k = 0; k < 4; ++k)
               if (c * 16 + 4 * k < sh.O3)
@@ -627,6 +653,94 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   }
   if (tid == 0 && *abort) atomicExch(p.status, (int)TR_ERR_TIMEOUT);
 
+  const size_t ybase = (size_t)t0 * sh.d_out;
+  if (lm) {
+    // ---- reduce over the cluster, lane-major: item e = float4 of column quad q = e / rows, row
+    // e % rows.  After the cluster barrier (release / acquire at cluster scope) rank r adds the
+    // CL areas' values of items [r SL, (r + 1) SL), every rank's load in flight at once, in rank
+    // order (the same order and sums as the row-major path), and writes y (one cluster per tile)
+    // or its workspace slot (NC > 1; the last cluster to finish adds the NC slots in cluster
+    // order).  Consecutive threads take consecutive rows: every load and slot access coalesces.
+    const int nq4 = sh.O3 >> 2;
+    const int nout = rows * o2n * nq4;
+    const int SL = (nout + p.CL - 1) / p.CL;
+    const int ebeg = crank * SL, eend = min(nout, ebeg + SL);
+    const size_t part4 = (size_t)p.part_elems / 4;
+    const float4* parts0 = reinterpret_cast<const float4*>(p.parts) + (size_t)(blockIdx.x - crank) * part4;
+    float4* slot = p.NC > 1
+        ? reinterpret_cast<float4*>(p.slots) +
+              (((size_t)tile * p.NG + grp) * p.NC + cl_id) * (size_t)(p.slot_elems / 4)
+        : nullptr;
+    const float4* s0 = reinterpret_cast<const float4*>(p.slots) +
+                       ((size_t)tile * p.NG + grp) * p.NC * (size_t)(p.slot_elems / 4);
+    auto store_y4 = [&](int e, float4 a) {
+      const int q = e / rows, r = e - q * rows;
+      const int o = q / nq4, o3 = (q - o * nq4) * 4;
+      const int t = r / sh.O1, o1 = r - t * sh.O1;
+      const size_t i = ybase + (size_t)t * sh.d_out + (size_t)o1 * sh.sy1 +
+                       (size_t)(o2a + o) * sh.sy2 + (size_t)o3 * sh.sy3;
+      const float f[4] = {a.x, a.y, a.z, a.w};
+      if (p.vec_out4) {
+        epi_store_vec<E, 4>(p.epi, p.y, i, f);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) epi_store<E>(p.epi, p.y, i + (size_t)k * sh.sy3, f[k]);
+      }
+    };
+    cluster.sync();
+    for (int e = ebeg + tid; e < eend; e += kTcThreads) {
+      const int q = e / rows, r = e - q * rows;
+      const float4* src = parts0 + (size_t)q * RS + r;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k0 = 0; k0 < p.CL; k0 += 8) {
+        float4 u[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (k0 + i < p.CL) u[i] = __ldcg(src + (size_t)(k0 + i) * part4);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (k0 + i < p.CL) {
+            a.x += u[i].x; a.y += u[i].y; a.z += u[i].z; a.w += u[i].w;
+          }
+        }
+      }
+      if (p.NC > 1) slot[e] = a;
+      else store_y4(e, a);
+    }
+    if (p.NC > 1) {
+      // ordering as in the row-major path below
+      __syncthreads();
+      int* counter = p.cnt + ((size_t)tile * p.NG + grp) * p.CL + crank;
+      if (tid == 0) {
+        __threadfence();
+        *flag = (atomicAdd(counter, 1) == p.NC - 1);
+        __threadfence();
+      }
+      __syncthreads();
+      if (*flag) {
+        const size_t sl4 = (size_t)(p.slot_elems / 4);
+        for (int e = ebeg + tid; e < eend; e += kTcThreads) {
+          float4 u[5];
+          float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int c0 = 0; c0 < p.NC; c0 += 5) {
+#pragma unroll
+            for (int i = 0; i < 5; ++i)
+              if (c0 + i < p.NC) u[i] = __ldcg(s0 + (size_t)(c0 + i) * sl4 + e);
+#pragma unroll
+            for (int i = 0; i < 5; ++i) {
+              if (c0 + i < p.NC) {
+                a.x += u[i].x; a.y += u[i].y; a.z += u[i].z; a.w += u[i].w;
+              }
+            }
+          }
+          store_y4(e, a);
+        }
+        if (tid == 0) atomicExch(counter, 0);
+      }
+    }
+    return;
+  }
+
   // ---- reduce over the cluster.  Items: 8 consecutive o3 (vector path) or single elements.
   // Every CTA writes its partial sums to its own workspace area (through L2: far faster than
   // distributed shared memory for this all-to-all), then after a cluster barrier (release /
@@ -649,7 +763,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
     for (int i = tid; i < rows * ystr / 4; i += kTcThreads) __stcg(dst + i, src[i]);
     cluster.sync();
   }
-  const size_t ybase = (size_t)t0 * sh.d_out;
   float* slot = p.NC > 1
       ? p.slots + (((size_t)tile * p.NG + grp) * p.NC + cl_id) * (size_t)p.slot_elems
       : nullptr;
@@ -836,6 +949,8 @@ static void fill_tc(TcParams<S>& tp, const Plan& p, const TcGeom& g, const void*
   const Canon& c = p.c;
   tp.vec_out = c.sy3 == 1 && c.O3 % 8 == 0 && c.sy1 % 8 == 0 && c.sy2 % 8 == 0 &&
                c.d_out % 8 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+  tp.vec_out4 = c.sy3 == 1 && c.O3 % 4 == 0 && c.sy1 % 4 == 0 && c.sy2 % 4 == 0 &&
+                c.d_out % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
   tp.slot_elems = 128 * t.O2G * p.c.O3;
   tp.spin_limit = p.wait_limit ? p.wait_limit : kSpinLimit;
 }

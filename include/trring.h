@@ -67,11 +67,16 @@ typedef struct tr_spec {
 
 /* Per-call kernel geometry override (tests and tuning).  Zero fields mean "planner's choice".
  *   tokens_per_tile : tokens per CTA row tile
- *   cluster         : CTAs per thread-block cluster that share one partial sum in DSMEM
+ *   cluster         : CTAs per thread-block cluster that split a tile's ring pieces and add
+ *                     their partial sums (through DSMEM in the decode kernel, through
+ *                     per-CTA workspace areas in L2 in the tcgen05 kernels)
  *   clusters        : clusters per row tile (>1 adds the workspace slot reduction)
  *   kernel          : 0 auto, 1 generic CUDA-core kernel, 2 mma.sync fused tile kernel,
- *                     3 tcgen05 fused kernel, 4 mma.sync decode kernel (T*o1 and T*i2 <= 32; here
- *                     `cluster` splits the pieces and `clusters` the output modes)          */
+ *                     3 tcgen05 fused kernel (ring rank padded to 8 or 16),
+ *                     4 mma.sync decode kernel (T*o1 and T*i2 <= 32; here `cluster` splits
+ *                     the pieces and `clusters` the output modes),
+ *                     5 tcgen05 slab kernel (the ring rank cut into slabs of 8; ranks up
+ *                     to 32)                                                               */
 typedef struct tr_tiling {
   int32_t tokens_per_tile;
   int32_t cluster;

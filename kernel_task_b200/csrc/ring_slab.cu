@@ -34,9 +34,9 @@
 // S3DONE) and one arrival per converter warp (D1READ: its TMEM loads landed, the buffer may be
 // overwritten; C1DONE / C2DONE: its operand slab is written).  Ring depths are chosen so that no
 // barrier can complete a phase twice before its consumer tests it.  After the last piece D3 is
-// summed across the cluster's CTAs through per-CTA workspace areas in L2 (and across clusters
-// through workspace slots when NC > 1) and written as y with the fused epilogue, exactly as in
-// ring_tc05.cu.  Launched with programmatic stream serialization: set-up and the first bulk
+// summed across the cluster's CTAs through per-CTA workspace areas in L2 (lane-major, written
+// straight from the TMEM loads) and across clusters through workspace slots when NC > 1, and
+// written as y with the fused epilogue, as in ring_tc05.cu.  Launched with programmatic stream serialization: set-up and the first bulk
 // copies of packed cores overlap the previous kernel; x, y and the workspace are touched only
 // after griddepcontrol.wait.
 //
@@ -104,7 +104,7 @@ struct SlabParams {
   int b1_bytes, b2_bytes, b3_bytes;
   int off_a2, off_b2, off_a3, off_a1, off_g1, off_b3, off_bar;
   int NA2, a2_bytes, NA3, a3_bytes, a1_bytes, NB1, b1_all, NB3, b3_all;
-  int ystr, vec_out, slot_elems, part_elems;
+  int ystr, vec_out, vec_out4, slot_elems, part_elems;
   int zero_a2;     // 1: A2 slots hold K columns C1 never writes (zeroed once)
   unsigned spin_limit;
   Epi epi;
@@ -569,11 +569,18 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
   }
 
   pdl_trigger();  // the next kernel may set up while this one reduces
-  // ---- D3 -> partial y of this CTA (rows (t,o1), columns (o of group, o3)), fp32 in smem.
-  // D3DONE: every tensor-core operation completed, so the operand space is free.
+  // ---- D3 -> partial y of this CTA (rows (t,o1), columns (o of group, o3)).
+  // Cluster of CTAs with O3 a multiple of 4 (lm): straight from the TMEM loads to this CTA's
+  // workspace area in L2, lane-major (float4 of column quad q = (o, o3 / 4) of row r at
+  // q * RS + r), so that the stores need no staging and every warp store covers 512 contiguous
+  // bytes.  Otherwise into shared memory (rows of ystr floats; the operand space is free once
+  // D3DONE has completed every tensor-core operation).
   __syncthreads();
   float* ys = reinterpret_cast<float*>(smem);
   const int ystr = p.ystr;
+  const bool lm = p.CL > 1 && (sh.O3 & 3) == 0;
+  const int RS = p.TT * sh.O1;  // rows of a tile: the row stride of the lane-major layout
+  float4* mine4 = reinterpret_cast<float4*>(p.parts + (size_t)blockIdx.x * p.part_elems);
   if (warp < 12) {
     const bool ok = np > 0 && mbar_spin(bar(SB_D3DONE), 0, abort, lim);
     tc_fence_after();
@@ -581,7 +588,8 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
     const bool vec4 = (sh.O3 & 3) == 0;
     const int nc16 = p.N3P / 16;
     for (int o = warp >> 2; o < o2n; o += 3) {
-      uint32_t v[4][16];  // all of this o's TMEM chunks (up to 64 o3) in flight at once
+      // all of this o's TMEM chunks in flight at once, one wait
+      uint32_t v[4][16];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         if (c < nc16 && ok) {
@@ -601,17 +609,35 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
 #pragma unroll
           for (int i = 0; i < 16; ++i) w[i] = 0u;
         }
-        if (r < rows)
-          for (int i = 0; i < 16; ++i)
-            if (c16 * 16 + i < sh.O3)
-              ys[r * ystr + o * sh.O3 + c16 * 16 + i] = __uint_as_float(w[i]);
+        if (r < rows) {
+          if (lm) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (c16 * 16 + 4 * k < sh.O3)
+                __stcg(mine4 + (size_t)(o * (sh.O3 >> 2) + c16 * 4 + k) * RS + r,
+                       make_float4(__uint_as_float(w[4 * k]), __uint_as_float(w[4 * k + 1]),
+                                   __uint_as_float(w[4 * k + 2]), __uint_as_float(w[4 * k + 3])));
+          } else {
+            for (int i = 0; i < 16; ++i)
+              if (c16 * 16 + i < sh.O3)
+                ys[r * ystr + o * sh.O3 + c16 * 16 + i] = __uint_as_float(w[i]);
+          }
+        }
       }
       if (r < rows) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           if (c >= nc16) break;
           float* dst = ys + r * ystr + o * sh.O3 + c * 16;
-          if (vec4) {
+          if (lm) {  // column quads (o, o3 / 4) of this row, lane-major: a warp store is 512 B
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (c * 16 + 4 * k < sh.O3)
+                __stcg(mine4 + (size_t)(o * (sh.O3 >> 2) + c * 4 + k) * RS + r,
+                       make_float4(__uint_as_float(v[c][4 * k]), __uint_as_float(v[c][4 * k + 1]),
+                                   __uint_as_float(v[c][4 * k + 2]),
+                                   __uint_as_float(v[c][4 * k + 3])));
+          } else if (vec4) {
 #pragma unroll
             for (int k = 0; k < 4; ++k)
               if (c * 16 + 4 * k < sh.O3)
@@ -627,6 +653,7 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
       }
     }
   }
+  if (lm) cluster_arrive_release();  // this CTA's partial sums are in L2; wait below
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {  // release TMEM: all reads completed (wait::ld) before the barrier
@@ -637,11 +664,98 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
   }
   if (tid == 0 && *abort) atomicExch(p.status, (int)TR_ERR_TIMEOUT);
 
+  const size_t ybase = (size_t)t0 * sh.d_out;
+  if (lm) {
+    // ---- reduce over the cluster, lane-major: item e = float4 of column quad q = e / rows, row
+    // e % rows.  After the cluster barrier (release / acquire at cluster scope) rank r adds the
+    // CL areas' values of items [r SLc, (r + 1) SLc), every rank's load in flight at once, in rank
+    // order (the same order and sums as the row-major path), and writes y (one cluster per tile)
+    // or its workspace slot (NC > 1; the last cluster to finish adds the NC slots in cluster
+    // order).  Consecutive threads take consecutive rows: every load and slot access coalesces.
+    const int nq4 = sh.O3 >> 2;
+    const int nout = rows * o2n * nq4;
+    const int SLc = (nout + p.CL - 1) / p.CL;
+    const int ebeg = crank * SLc, eend = min(nout, ebeg + SLc);
+    const size_t part4 = (size_t)p.part_elems / 4;
+    const float4* parts0 = reinterpret_cast<const float4*>(p.parts) + (size_t)(blockIdx.x - crank) * part4;
+    float4* slot = p.NC > 1
+        ? reinterpret_cast<float4*>(p.slots) +
+              (((size_t)tile * p.NG + grp) * p.NC + cl_id) * (size_t)(p.slot_elems / 4)
+        : nullptr;
+    const float4* s0 = reinterpret_cast<const float4*>(p.slots) +
+                       ((size_t)tile * p.NG + grp) * p.NC * (size_t)(p.slot_elems / 4);
+    auto store_y4 = [&](int e, float4 a) {
+      const int q = e / rows, r = e - q * rows;
+      const int o = q / nq4, o3 = (q - o * nq4) * 4;
+      const int t = r / sh.O1, o1 = r - t * sh.O1;
+      const size_t i = ybase + (size_t)t * sh.d_out + (size_t)o1 * sh.sy1 +
+                       (size_t)(o2a + o) * sh.sy2 + (size_t)o3 * sh.sy3;
+      const float f[4] = {a.x, a.y, a.z, a.w};
+      if (p.vec_out4) {
+        epi_store_vec<E, 4>(p.epi, p.y, i, f);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) epi_store<E>(p.epi, p.y, i + (size_t)k * sh.sy3, f[k]);
+      }
+    };
+    cluster_wait_acquire();
+    for (int e = ebeg + tid; e < eend; e += kSlThreads) {
+      const int q = e / rows, r = e - q * rows;
+      const float4* src = parts0 + (size_t)q * RS + r;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k0 = 0; k0 < p.CL; k0 += 8) {
+        float4 u[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (k0 + i < p.CL) u[i] = __ldcg(src + (size_t)(k0 + i) * part4);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (k0 + i < p.CL) {
+            a.x += u[i].x; a.y += u[i].y; a.z += u[i].z; a.w += u[i].w;
+          }
+        }
+      }
+      if (p.NC > 1) slot[e] = a;
+      else store_y4(e, a);
+    }
+    if (p.NC > 1) {
+      // the CTA barrier gathers every thread's slot stores; thread 0's acq_rel arrival
+      // publishes them at device scope and, for the last cluster, acquires the other clusters'
+      // slots, which the second CTA barrier passes on to every thread
+      __syncthreads();
+      int* counter = p.cnt + ((size_t)tile * p.NG + grp) * p.CL + crank;
+      if (tid == 0) *flag = (atom_add_acq_rel_gpu(counter, 1) == p.NC - 1);
+      __syncthreads();
+      if (*flag) {
+        const size_t sl4 = (size_t)(p.slot_elems / 4);
+        for (int e = ebeg + tid; e < eend; e += kSlThreads) {
+          float4 u[5];
+          float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int c0 = 0; c0 < p.NC; c0 += 5) {
+#pragma unroll
+            for (int i = 0; i < 5; ++i)
+              if (c0 + i < p.NC) u[i] = __ldcg(s0 + (size_t)(c0 + i) * sl4 + e);
+#pragma unroll
+            for (int i = 0; i < 5; ++i) {
+              if (c0 + i < p.NC) {
+                a.x += u[i].x; a.y += u[i].y; a.z += u[i].z; a.w += u[i].w;
+              }
+            }
+          }
+          store_y4(e, a);
+        }
+        if (tid == 0) atomicExch(counter, 0);
+      }
+    }
+    return;
+  }
+
   // ---- reduce over the cluster.  Items: 8 consecutive o3 (vector path) or single elements.
-  // Every CTA writes its partial sums to its own workspace area (through L2), then after a
-  // cluster barrier (release / acquire at cluster scope) cluster rank r adds items
-  // [r SL, (r + 1) SL) of the CL areas in rank order and writes y (one cluster per tile) or its
-  // workspace slot (NC > 1; the last cluster to finish adds the NC slots in cluster order).
+  // Every CTA writes its partial sums to its own workspace area (through L2: far faster than
+  // distributed shared memory for this all-to-all), then after a cluster barrier (release /
+  // acquire at cluster scope) cluster rank r adds items [r SLc, (r + 1) SLc) of the CL areas in
+  // rank order and writes y (one cluster per tile) or its workspace slot (NC > 1; the last
+  // cluster to finish adds the NC slots in cluster order).
   const int W = p.vec_out ? 8 : 1;  // floats per item
   const int nper = p.vec_out ? sh.O3 / 8 : sh.O3;
   const int nout = rows * o2n * nper;
@@ -658,12 +772,12 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
     for (int i = tid; i < rows * ystr / 4; i += kSlThreads) __stcg(dst + i, src[i]);
     cluster.sync();
   }
-  const size_t ybase = (size_t)t0 * sh.d_out;
   float* slot = p.NC > 1
       ? p.slots + (((size_t)tile * p.NG + grp) * p.NC + cl_id) * (size_t)p.slot_elems
       : nullptr;
   const float* s0 = p.slots + ((size_t)tile * p.NG + grp) * p.NC * (size_t)p.slot_elems;
-  auto store_y = [&](int e, const float* f) {  // the 8 (or 1) finished values of item e
+  // write the 8 (or 1) finished values of item e to y
+  auto store_y = [&](int e, const float* f) {
     const int o3v = e % nper, q = e / nper;
     const int o = q % o2n, r = q / o2n;
     const int t = r / sh.O1, o1 = r - t * sh.O1;
@@ -849,6 +963,8 @@ static void fill_slab(SlabParams<S>& sp, const Plan& p, const SlabGeom& g, const
   const Canon& c = p.c;
   sp.vec_out = c.sy3 == 1 && c.O3 % 8 == 0 && c.sy1 % 8 == 0 && c.sy2 % 8 == 0 &&
                c.d_out % 8 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+  sp.vec_out4 = c.sy3 == 1 && c.O3 % 4 == 0 && c.sy1 % 4 == 0 && c.sy2 % 4 == 0 &&
+                c.d_out % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
   sp.slot_elems = 128 * l.O2G * c.O3;
   sp.spin_limit = p.wait_limit ? p.wait_limit : kSpinLimit;
 }

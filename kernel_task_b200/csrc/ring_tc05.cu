@@ -643,6 +643,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
       }
     }
   }
+  if (lm) cluster_arrive_release();  // this CTA's partial sums are in L2; wait below
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {  // release TMEM: all reads completed (wait::ld) before the barrier
@@ -687,7 +688,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
         for (int k = 0; k < 4; ++k) epi_store<E>(p.epi, p.y, i + (size_t)k * sh.sy3, f[k]);
       }
     };
-    cluster.sync();
+    cluster_wait_acquire();
     for (int e = ebeg + tid; e < eend; e += kTcThreads) {
       const int q = e / rows, r = e - q * rows;
       const float4* src = parts0 + (size_t)q * RS + r;
@@ -708,14 +709,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
       else store_y4(e, a);
     }
     if (p.NC > 1) {
-      // ordering as in the row-major path below
+      // the CTA barrier gathers every thread's slot stores; thread 0's acq_rel arrival
+      // publishes them at device scope and, for the last cluster, acquires the other clusters'
+      // slots, which the second CTA barrier passes on to every thread
       __syncthreads();
       int* counter = p.cnt + ((size_t)tile * p.NG + grp) * p.CL + crank;
-      if (tid == 0) {
-        __threadfence();
-        *flag = (atomicAdd(counter, 1) == p.NC - 1);
-        __threadfence();
-      }
+      if (tid == 0) *flag = (atom_add_acq_rel_gpu(counter, 1) == p.NC - 1);
       __syncthreads();
       if (*flag) {
         const size_t sl4 = (size_t)(p.slot_elems / 4);

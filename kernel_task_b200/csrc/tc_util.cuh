@@ -199,6 +199,29 @@ __device__ __forceinline__ void named_arrive(int id, int n) {
   asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(n) : "memory");
 }
 
+// The two halves of a cluster barrier, so that work between them overlaps its latency: every
+// thread's earlier memory accesses are released at cluster scope by the arrive and acquired
+// by the wait (both executed by every thread of the CTA, warps converged).
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+// Arrival on a device-scope counter: returns the previous value.  Release: called by one thread
+// after a CTA barrier, it publishes the writes that every thread of the CTA made before the
+// barrier; acquire: the caller (and, after a following CTA barrier, every thread) sees the
+// writes that the earlier arrivals published.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;\n"
+               : "=r"(old)
+               : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
 template <int N>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]);
 template <>

@@ -13,7 +13,9 @@
 // D1 and D2 live either in separate TMEM buffers (one or two D1, two D2) or, when that makes the
 // o2 groups wider, in two shared buffers that hold a piece's D1 and then its D2.
 // Roles (512 threads):
-//   warps 0-7   C1 (warps w and w+4 read the same TMEM lanes, each half of the o1 range)
+//   warps 0-7   C1 (warps w and w+4 read the same TMEM lanes: alternate pieces, each the whole
+//               o1 range, when D1 has two buffers of its own; else each half of every piece's
+//               o1 range)
 //   warps 8-11  C2, and the D3 read-out with warps 0-7 after the last piece
 //   warp 12     S2 issuer: S2 of each piece
 //   warp 13     S3 issuer: S3 of each piece
@@ -60,6 +62,10 @@ namespace cg = cooperative_groups;
 
 namespace trr {
 
+#ifndef TRR_C1_ALT
+#define TRR_C1_ALT 1
+#endif
+
 constexpr int kTcThreads = 512;
 constexpr int kBuildThreads = 416;  // converter and feeder warps: first x slices
 constexpr unsigned kPollLimit = 1u << 24;    // loader polls without progress before it gives up
@@ -97,6 +103,7 @@ struct TcParams {
   int* status;
   int T, TT, CL, NC, NG, O2G;
   int shared_d12, ND1, DBW, N1P, N2, N3P, d2_col, d3_col, tmem_cols;
+  int c1_alt;  // the two C1 warp groups take alternate pieces (see the C1 loop)
   int b1_bytes, b2_bytes, b3_bytes;
   int off_a2, off_b2, off_a3, off_a1, off_g1, off_b3, off_bar;
   int NA2, NA3, NB1, b1_all, NB3, b3_all, a2_bytes, a3_bytes, a1_bytes;
@@ -218,7 +225,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
       if ((i >= BAR_D2READ && i < BAR_D2READ + 2) || (i >= BAR_C2DONE && i < BAR_C2DONE + 2))
         count = 4;
       if ((i >= BAR_C1DONE && i < BAR_C1DONE + 2) || (i >= BAR_D1READ && i < BAR_D1READ + 2))
-        count = 8;
+        count = p.c1_alt ? 4 : 8;
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar(i)), "r"(count)
                    : "memory");
     }
@@ -387,11 +394,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
       const int r1 = 32 * (warp & 3) + lane;  // D1 row (t, i2)
       const int tq = r1 / sh.I2, i2 = r1 - tq * sh.I2;
       const bool rvalid = tq < p.TT;
+      // c1_alt: warps 0-3 convert the even pieces and warps 4-7 the odd ones, each the whole o1
+      // range (two pieces in flight, for a step bound by latency: the TMEM load wait and the
+      // proxy fence); otherwise warps w and w + 4 split each piece's o1 range
       const int h = (sh.O1 + 1) >> 1;
-      const int o1a = (warp >> 2) ? h : 0, o1b = (warp >> 2) ? sh.O1 : h;
+      const int o1a = p.c1_alt ? 0 : ((warp >> 2) ? h : 0);
+      const int o1b = p.c1_alt ? sh.O1 : ((warp >> 2) ? sh.O1 : h);
       const int rot = NCH == 2 ? ((i2 >> 2) & 1) : 0;
       bool ok = true;
-      for (int j = 0; j < np; ++j) {
+      const int jstep = p.c1_alt ? 2 : 1;
+      for (int j = p.c1_alt ? (warp >> 2) : 0; j < np; j += jstep) {
         const int ab = j % p.NA2;
         if (ok) ok = mbar_spin(bar(BAR_S1DONE + (j & 3)), (j >> 2) & 1, abort, p.spin_limit);
         if (ok && j >= p.NA2)  // S2 of the piece that last used this A2 buffer completed
@@ -915,6 +927,9 @@ static void fill_tc(TcParams<S>& tp, const Plan& p, const TcGeom& g, const void*
   tp.NG = t.NG;
   tp.O2G = t.O2G;
   tp.shared_d12 = t.shared_d12;
+  // alternate pieces between the C1 groups when D1 has two buffers of its own (c1 T32 26.1 ->
+  // 24.4 us; with D1 and D2 sharing two buffers, as for c2, it measured 2 us slower)
+  tp.c1_alt = TRR_C1_ALT && t.ND1 >= 2 && !t.shared_d12 ? 1 : 0;
   tp.ND1 = t.ND1;
   tp.DBW = t.DBW;
   tp.N1P = t.N1P;

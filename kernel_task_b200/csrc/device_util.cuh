@@ -65,6 +65,24 @@ __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
 
+// Hint: bring the whole 16-byte units inside [p, p + bytes) into L2 (the start is rounded up
+// and the end down, so nothing outside the range is touched).  Only a hint: L2 is the point of
+// coherence, so it may be issued before griddepcontrol.wait even for data the previous kernel
+// is still writing; the loads that follow the wait see the written values.
+__device__ __forceinline__ void prefetch_l2(const void* p, size_t bytes) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uintptr_t b = (a + 15) & ~(uintptr_t)15, e = (a + bytes) & ~(uintptr_t)15;
+  if (e <= b) return;
+  bytes = e - b;
+  const char* c = reinterpret_cast<const char*>(b);
+  while (bytes > 0) {  // one bulk prefetch covers at most 2^20 - 16 bytes here
+    const uint32_t n = (uint32_t)(bytes < ((1u << 20) - 16) ? bytes : ((1u << 20) - 16));
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(c), "r"(n) : "memory");
+    c += n;
+    bytes -= n;
+  }
+}
+
 // ---- output epilogue (struct Epi, plan.h): the value written for y[i], and the store
 template <typename E, class EP>
 __device__ __forceinline__ float epi_value(const EP& ep, size_t i, float v) {

@@ -236,6 +236,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
     if (lane == 0) {
       *flag = 0;
       *abort = 0;
+      // L2 prefetch (a hint, see prefetch_l2): the tile's x rows, gathered right after
+      // griddepcontrol.wait, and the slot counter of the reduction
+      prefetch_l2(xt, (size_t)TTv * sh.d_in * 2);
+      if (p.NC > 1)  // the 16-byte unit holding the counter (the counter area is 256-byte
+                     // aligned and padded to 256 bytes)
+        prefetch_l2(p.cnt + ((((size_t)tile * p.NG + grp) * p.CL + crank) & ~(size_t)3), 16);
       if (np > 0) {  // the feeder's first bulk copies go out at once
         bulk_load(b2s, p.b2 + (size_t)grp * p.b2_bytes, p.b2_bytes, bar(BAR_B2FULL));
         if (p.b1_all) {

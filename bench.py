@@ -10,8 +10,11 @@ Per case:
                 around the call on the launching stream: device time of a cold-cache call.
   warm leg      the reference harness's protocol: 5 blocks x 20 back-to-back calls, median
                 (benchmarks/benchmark.py:163-174).
-  e2e leg       the public API end to end: pinned host x -> device, fn(x), y -> pinned host,
-                after an L2 flush and with the GPU idle, so host dispatch is inside the region.
+  e2e leg       the public API end to end on host buffers: pinned host x -> device, the
+                operator, y -> pinned host, after an L2 flush and with the GPU idle, so host
+                dispatch is inside the region.  Our operator takes the host buffers in one call
+                (fn.forward_host: tr_forward_host issues both copies and the kernel); the same
+                through torch copies around fn(x) is reported beside it (e2e_torch_copies_us).
   dense bar     F.linear(x, W) on the materialised fp16 W, same legs (TF32 off).
   reference     the reference's own PreparedTRKernel (its tr_ring.cu built for sm_100 by
                 baseline/build_reference.py) in a child process: default dispatch, and with the
@@ -224,20 +227,28 @@ def warm_stream_us(fn, x, blocks=5, per_block=20):
     return statistics.median(out)
 
 
-def e2e_us(fn, x_host, flush, steps, warmup, d_out):
-    """Public API end to end: pinned x -> device, fn, y -> pinned host, GPU idle at start."""
+def e2e_us(fn, x_host, flush, steps, warmup, d_out, host_call=True):
+    """Public API end to end with host buffers: pinned x -> device, the operator, y -> pinned
+    host, the GPU idle and L2 flushed at the start of every step.  With host_call, our operator
+    takes the host buffers in one call, fn.forward_host(x, out=y) (tr_forward_host: both copies
+    and the kernel); otherwise torch copies around fn(x) (the dense bar, and our operator for
+    comparison)."""
     dev = flush.device
     x_dev = torch.empty(x_host.shape, dtype=x_host.dtype, device=dev)
     y_host = torch.empty((x_host.shape[0], d_out), dtype=x_host.dtype, pin_memory=True)
+    direct = host_call and hasattr(fn, "forward_host")
     res = []
     for i in range(warmup + steps):
         flush.add_(1)
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        x_dev.copy_(x_host, non_blocking=True)
-        y = fn(x_dev)
-        y_host.copy_(y, non_blocking=True)
+        if direct:
+            fn.forward_host(x_host, y_host)
+        else:
+            x_dev.copy_(x_host, non_blocking=True)
+            y = fn(x_dev)
+            y_host.copy_(y, non_blocking=True)
         e.record()
         e.synchronize()
         if i >= warmup:
@@ -813,6 +824,10 @@ def run_ours(args, rank, world, local_rank):
         e2e, c["h2d"], c["d2h"] = e2e_us(c["fn"], xh, flush, steps, warmup,
                                           c["spec"].out_features)
         c["e2e"] = e2e
+        # the same through torch copies around fn(x) (three host dispatches)
+        c["e2e_torch_copies"] = statistics.mean(e2e_us(c["fn"], xh, flush, steps, warmup,
+                                                       c["spec"].out_features,
+                                                       host_call=False)[0])
         if not args.no_dense:
             W = dense_weight(c["cores"])
             dfn = lambda v, W=W: torch.nn.functional.linear(v, W)  # noqa: E731
@@ -868,7 +883,9 @@ def run_ours(args, rank, world, local_rank):
         rec = {
             "us": round(mean[i], 3), "us_median": round(med[i], 3),
             "warm_stream_us": round(c["warm"], 3), "host_latency_us": round(c["host"], 2),
-            "e2e_us": round(e2e[i], 3), "prep_ms": round(c["prep_ms"], 2),
+            "e2e_us": round(e2e[i], 3),
+            "e2e_torch_copies_us": round(c["e2e_torch_copies"], 3),
+            "prep_ms": round(c["prep_ms"], 2),
             "kernel": KERNEL_NAMES.get(c["tiling"]["kernel"], "?"),
             "dense_us": round(c.get("dense_cold", float("nan")), 3),
             "dense_warm_stream_us": round(c.get("dense_warm", float("nan")), 3),

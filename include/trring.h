@@ -131,6 +131,19 @@ int tr_plan_set_wait_limit(tr_plan* plan, uint32_t polls);
 int tr_forward(const tr_plan* plan, const void* packed, const void* x, int64_t tokens, void* y,
                void* workspace, size_t workspace_bytes, void* stream);
 
+/* tr_forward on host buffers: x_host [tokens, d_in] is copied into the device staging buffer
+ * x_dev, the forward writes y_dev, and y_dev is copied into y_host [tokens, d_out], as three
+ * stream-ordered operations (two cudaMemcpyAsync and one kernel) issued by one call.  The call
+ * returns before they finish: synchronise `stream` before reading y_host.  Page-locked host
+ * memory keeps the copies asynchronous.  x_dev and y_dev are caller-owned device buffers of at
+ * least tokens * d_in and tokens * d_out elements, 16-byte aligned; they may be reused by the
+ * next call on the same stream.  For hosts whose data lives in host memory (a plugin, another
+ * language's FFI); the reference's callers always pass device tensors, so it has no
+ * counterpart there.                                                                          */
+int tr_forward_host(const tr_plan* plan, const void* packed, const void* x_host, int64_t tokens,
+                    void* y_host, void* x_dev, void* y_dev, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
 /* Same as tr_forward with an explicit geometry (NULL = planner's choice). */
 int tr_forward_tiled(const tr_plan* plan, const void* packed, const void* x, int64_t tokens,
                      void* y, void* workspace, size_t workspace_bytes, const tr_tiling* tiling,

@@ -52,6 +52,8 @@ PROTOTYPES = {
     "tr_forward_tiled": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
                                  c_size_t, POINTER(TrTiling), c_void_p]),
     "tr_forward_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
+    "tr_forward_host": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
+                                c_void_p, c_void_p, c_size_t, c_void_p]),
     "tr_forward_epilogue": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
                                     POINTER(TrEpilogue), c_void_p, c_size_t, POINTER(TrTiling),
                                     c_void_p]),
@@ -140,6 +142,16 @@ class Plan:
         return lib().tr_forward_tiled(self.handle, c_void_p(packed_ptr), c_void_p(x_ptr), tokens,
                                       c_void_p(y_ptr), c_void_p(ws_ptr or None), ws_bytes,
                                       ctypes.byref(tiling) if tiling else None, c_void_p(stream))
+
+    def forward_host(self, packed_ptr: int, x_host_ptr: int, tokens: int, y_host_ptr: int,
+                     x_dev_ptr: int, y_dev_ptr: int, ws_ptr: int = 0, ws_bytes: int = 0,
+                     stream: int = 0) -> int:
+        """tr_forward on host buffers through caller-owned device staging (three stream-ordered
+        operations; synchronise before reading y)."""
+        return lib().tr_forward_host(self.handle, c_void_p(packed_ptr), c_void_p(x_host_ptr),
+                                     tokens, c_void_p(y_host_ptr), c_void_p(x_dev_ptr),
+                                     c_void_p(y_dev_ptr), c_void_p(ws_ptr or None), ws_bytes,
+                                     c_void_p(stream))
 
     def forward_noalloc(self, packed_ptr: int, x_ptr: int, tokens: int, y_ptr: int,
                         stream: int = 0) -> int:

@@ -1291,6 +1291,44 @@ int tr_forward(const tr_plan* plan, const void* packed, const void* x, int64_t t
   return tr_forward_tiled(plan, packed, x, tokens, y, workspace, workspace_bytes, nullptr, stream);
 }
 
+int tr_forward_host(const tr_plan* plan, const void* packed, const void* x_host, int64_t tokens,
+                    void* y_host, void* x_dev, void* y_dev, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  if (!plan) {
+    set_error("null plan");
+    return TR_ERR_INVALID;
+  }
+  if (tokens < 0) {
+    set_error("negative token count");
+    return TR_ERR_INVALID;
+  }
+  if (tokens == 0) return TR_OK;
+  if (!x_host || !y_host || !x_dev || !y_dev) {
+    set_error("null host buffer or device staging buffer");
+    return TR_ERR_INVALID;
+  }
+  const size_t es = elem_size(plan->dtype);
+  const size_t xb = (size_t)tokens * plan->c.d_in * es;
+  const size_t yb = (size_t)tokens * plan->c.d_out * es;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(x_dev, x_host, xb, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("copy of x to the device: %s", cudaGetErrorString(e));
+    return TR_ERR_CUDA;
+  }
+  const int s = tr_forward_tiled(plan, packed, x_dev, tokens, y_dev, workspace, workspace_bytes,
+                                 nullptr, stream);
+  if (s != TR_OK) return s;
+  e = cudaMemcpyAsync(y_host, y_dev, yb, cudaMemcpyDeviceToHost, st);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("copy of y to the host: %s", cudaGetErrorString(e));
+    return TR_ERR_CUDA;
+  }
+  return TR_OK;
+}
+
 int tr_forward_noalloc(const tr_plan* plan, const void* packed, const void* x, int64_t tokens,
                        void* y, void* stream) {
   if (!plan) {

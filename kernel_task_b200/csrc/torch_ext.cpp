@@ -7,6 +7,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
 #include <torch/extension.h>
 
 #include <cstdlib>
@@ -172,6 +173,59 @@ class RingOp {
 
   at::Tensor call(const at::Tensor& x) { return forward_impl(x, nullptr); }
 
+  // y = TR(x) for a host-resident x (tr_forward_host): one call issues the copy of x to the
+  // device, the forward and the copy of y back, on the current stream, and returns `out` (or a
+  // new page-locked tensor) before they finish: synchronise the stream before reading it.  The
+  // device staging buffers belong to this object and are reused by its next call.
+  at::Tensor forward_host(const at::Tensor& x, c10::optional<at::Tensor> out) {
+    if (x.dim() != 2 || x.size(1) != d_in_)
+      throw py::value_error("Expected x with shape [tokens, " + std::to_string(d_in_) + "]");
+    if (x.is_cuda()) throw py::value_error("forward_host takes x in host memory");
+    if (x.scalar_type() != dtype_) throw py::value_error("x dtype must match the cores");
+    if (!x.is_contiguous()) throw py::value_error("x must be contiguous");
+    if (!packed_.defined()) throw std::runtime_error("cores are not packed");
+    const int64_t T = x.size(0);
+    at::Tensor y;
+    if (out.has_value()) {
+      y = *out;
+      if (y.is_cuda() || y.dim() != 2 || y.size(0) != T || y.size(1) != d_out_ ||
+          y.scalar_type() != dtype_ || !y.is_contiguous())
+        throw py::value_error("out must be a contiguous host tensor [tokens, " +
+                              std::to_string(d_out_) + "] of the cores' dtype");
+    } else {
+      y = at::empty({T, d_out_}, x.options().pinned_memory(true));
+    }
+    if (T == 0) return y;
+    c10::cuda::OptionalCUDAGuard guard;
+    if (c10::cuda::current_device() != device_) guard.set_index((c10::DeviceIndex)device_);
+    const auto dev = at::TensorOptions().dtype(at::kByte).device(at::kCUDA,
+                                                                  (c10::DeviceIndex)device_);
+    const size_t es = x.element_size();
+    const size_t xb = (size_t)T * d_in_ * es, yb = (size_t)T * d_out_ * es;
+    if (xb > xs_bytes_) {
+      xs_ = at::empty({(int64_t)xb}, dev);
+      xs_bytes_ = xb;
+    }
+    if (yb > ys_bytes_) {
+      ys_ = at::empty({(int64_t)yb}, dev);
+      ys_bytes_ = yb;
+    }
+    size_t need = 0;
+    int st = tr_workspace_bytes(plan_.get(), T, &need);
+    if (st != TR_OK) raise_status(st, "tr_workspace_bytes");
+    if (need > ws_bytes_) {
+      ws_ = at::zeros({(int64_t)need}, dev);
+      ws_bytes_ = need;
+    }
+    cudaStream_t stream = at::cuda::getCurrentCUDAStream((c10::DeviceIndex)device_).stream();
+    st = tr_forward_host(plan_.get(), packed_.data_ptr(), x.data_ptr(), T, y.data_ptr(),
+                         xs_.data_ptr(), ys_.data_ptr(), ws_bytes_ ? ws_.data_ptr() : nullptr,
+                         ws_bytes_, stream);
+    if (st != TR_OK) raise_status(st, "tr_forward_host");
+    if (check_status_) check_device_status();
+    return y;
+  }
+
   // y in fp32, no rounding to the cores' dtype (the reference's accumulate / forward_fp32)
   at::Tensor accumulate(const at::Tensor& x) {
     return forward_impl(x, nullptr, TR_EPI_NONE, nullptr, true);
@@ -255,6 +309,8 @@ class RingOp {
   at::Tensor packed_;
   at::Tensor ws_;
   size_t ws_bytes_ = 0;
+  at::Tensor xs_, ys_;  // device staging of forward_host
+  size_t xs_bytes_ = 0, ys_bytes_ = 0;
   bool check_status_ = false;
 };
 
@@ -309,6 +365,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            py::arg("device"))
       .def("pack", &RingOp::pack)
       .def("__call__", &RingOp::call)
+      .def("forward_host", &RingOp::forward_host, py::arg("x"), py::arg("out") = py::none())
       .def("accumulate", &RingOp::accumulate)
       .def("forward_add", &RingOp::forward_add, py::arg("x"), py::arg("h"))
       .def("forward_silu_mul", &RingOp::forward_silu_mul, py::arg("x"), py::arg("g"))

@@ -294,6 +294,67 @@ def test_c_abi_direct_on_current_stream(golden):
     check_close(y, golden[f"{key}_yref_t8"], torch.float16)
 
 
+@pytest.mark.parametrize("R", [8, 16])
+def test_forward_host_equals_device_call(golden, R):
+    """forward_host (tr_forward_host: host x and y, device staging owned by the operator) gives
+    the device call's y bit for bit, at every suite token count and with the staging reused
+    across token counts; into a caller's page-locked `out` or a new one; the empty batch; and
+    the reference's vectors."""
+    key = f"req_r{R}"
+    cores = golden_cores(golden, key, torch.float16)
+    fn = prepare_optimized(cores, kspec.TRSpec(rank=R))
+    for T in (32, 1, 8, 0):
+        x = kspec.baseline_x(kspec.TRSpec(rank=R), T, seed=T, dtype=torch.float16, device=DEV)
+        xh = x.cpu().pin_memory()
+        out = torch.empty(T, 2880, dtype=torch.float16).pin_memory()
+        y = fn.forward_host(xh, out)
+        assert y.data_ptr() == out.data_ptr()
+        y2 = fn.forward_host(xh)
+        torch.cuda.synchronize()
+        assert not y2.is_cuda and (T == 0 or y2.is_pinned())  # an empty tensor has no storage
+        want = fn(x).cpu()
+        torch.testing.assert_close(y, want, rtol=0, atol=0)
+        torch.testing.assert_close(y2, want, rtol=0, atol=0)
+    for T in (1, 8, 32):
+        if f"{key}_x_t{T}" in golden:
+            xh = torch.from_numpy(np.ascontiguousarray(golden[f"{key}_x_t{T}"])).half()
+            y = fn.forward_host(xh.pin_memory())
+            torch.cuda.synchronize()
+            check_close(y, golden[f"{key}_yref_t{T}"], torch.float16)
+    with pytest.raises(ValueError):
+        fn.forward_host(torch.zeros(2, 1920, dtype=torch.float16, device=DEV))
+    with pytest.raises(ValueError):
+        fn.forward_host(torch.zeros(2, 1920, dtype=torch.float16),
+                        torch.empty(3, 2880, dtype=torch.float16))
+
+
+def test_forward_host_c_abi(golden):
+    """tr_forward_host through ctypes with caller-owned staging on a side stream."""
+    key = "req_r8"
+    cores = golden_cores(golden, key, torch.float16)
+    plan = abi.Plan((8, 12, 20), (12, 10, 24), 8, abi.TR_F16, torch.cuda.current_device())
+    packed = torch.empty(plan.packed_bytes(), dtype=torch.uint8, device=DEV)
+    stream = torch.cuda.Stream()
+    xh = torch.from_numpy(np.ascontiguousarray(golden[f"{key}_x_t8"])).half().pin_memory()
+    yh = torch.empty(8, 2880, dtype=torch.float16).pin_memory()
+    xd = torch.empty(8, 1920, dtype=torch.float16, device=DEV)
+    yd = torch.empty(8, 2880, dtype=torch.float16, device=DEV)
+    with torch.cuda.stream(stream):
+        plan.pack([c.data_ptr() for c in cores], packed.data_ptr(), stream.cuda_stream)
+        need = plan.workspace_bytes(8)
+        ws = torch.zeros(max(need, 16), dtype=torch.uint8, device=DEV)
+        assert plan.forward_host(packed.data_ptr(), xh.data_ptr(), 8, yh.data_ptr(), 0,
+                                 yd.data_ptr(), ws.data_ptr(), need,
+                                 stream.cuda_stream) == abi.TR_ERR_INVALID
+        for _ in range(2):
+            st = plan.forward_host(packed.data_ptr(), xh.data_ptr(), 8, yh.data_ptr(),
+                                   xd.data_ptr(), yd.data_ptr(), ws.data_ptr(), need,
+                                   stream.cuda_stream)
+            assert st == abi.TR_OK
+    stream.synchronize()
+    check_close(yh, golden[f"{key}_yref_t8"], torch.float16)
+
+
 def test_generic_fp32_kernel_cross_checks_mma():
     """Independent GPU path: fp32 plan (generic CUDA-core kernel) on the fp16 values."""
     s = kspec.SPEC_C1

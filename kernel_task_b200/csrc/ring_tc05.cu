@@ -164,7 +164,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
   const S& sh = p.sh;
   constexpr int K3 = 16;         // S3 K (v padded to 16)
   constexpr int NCH = RP / 8;    // 16-byte chunks of one (o1 or o2, i2) run of RP values
-  constexpr int CB = 5;          // 16-column TMEM loads per wait in C1 (80 columns)
+  // 16-column TMEM loads per wait in C1 (64 columns).  Measured on the 65,536-token config-5
+  // prefill (128 columns per thread, two waits): 4 -> 190 ms, 5 -> 203 ms, 3 -> 209 ms,
+  // 2 -> 213 ms; the config-1/2 cases within 0.2 us of each other.
+#ifndef TRR_CB
+#define TRR_CB 4
+#endif
+  constexpr int CB = TRR_CB;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -418,7 +424,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
         if (ok) {
           unsigned char* a2 = smem + p.off_a2 + ab * p.a2_bytes;
           const uint32_t d1 = tmem + lane_base + d1_col(j);
-          // D1 columns (o1, u) of this warp's o1 half, 16 per TMEM load, up to 80 per wait;
+          // D1 columns (o1, u) of this warp's o1 half, 16 per TMEM load, CB loads per wait;
           // a load may run past the half (never past the allocation): those columns are unused
           const int cb0 = o1a * RP, ce = o1b * RP;
           for (int cb = cb0; cb < ce; cb += 16 * CB) {

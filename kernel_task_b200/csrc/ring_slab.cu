@@ -468,7 +468,9 @@ __global__ void __launch_bounds__(kSlThreads, 1) ring_slab_kernel(const SlabPara
           const uint32_t d2 = tmem + lane_base + d2_col(j);
           unsigned char* rowp = smem + p.off_a3 + ab * p.a3_bytes +
                                 (r >> 3) * ((p.K3P / 8) * 128) + (r & 7) * 16;
-          constexpr int CB2 = 4;
+          // six 16-column loads per wait: config 3's 96 D2 columns in one wait (c3 T = 128
+          // 2.80 -> 2.58 ms against four)
+          constexpr int CB2 = 6;
           // D2 column = o * RV + v, walked in 8-column chunks: (o, vv) advance without division
           int o = 0, vv = 0;
           for (int c0 = 0; c0 < p.N2; c0 += 16 * CB2) {

@@ -47,7 +47,7 @@
 //
 // Every wait is bounded (SlabParams::spin_limit polls); on expiry the CTA raises a shared abort
 // flag (later waits return at once), records TR_ERR_TIMEOUT in the first workspace word, waits
-// for its own bulk copies, and returns; the two issuing warps always wait for their own
+// for its own bulk copies, and returns; the three issuing warps always wait for their own
 // tensor-core work before the barrier that precedes the TMEM release.
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>

@@ -45,7 +45,7 @@
 // Every wait on an mbarrier is bounded (TcParams::spin_limit polls); on expiry the CTA raises a
 // shared abort flag (all later waits return at once), records TR_ERR_TIMEOUT in the status word
 // (the first workspace word, read by tr_workspace_status), waits (bounded) for its own bulk
-// copies in flight, and returns.  The two issuing warps always wait for their own tensor-core
+// copies in flight, and returns.  The three issuing warps always wait for their own tensor-core
 // work before the CTA barrier that precedes the TMEM release.
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
@@ -82,7 +82,7 @@ enum {
   BAR_B3FULL = 32,  // [16] B3 landed (slot 0 only when the whole range loads at once)
   BAR_B2FULL = 48,  // B2 landed
   BAR_D3DONE = 49,  // commit after the last S3: every tensor-core operation completed
-  BAR_DRAIN = 50,   // [2] after the piece loop: the two issuing warps' own work completed
+  BAR_DRAIN = 50,   // [2] after the piece loop: the S2 and S3 issuers' own work completed
   BAR_C1DONE = 52,  // [2] C1 warps finished piece j (count 8), index j % 2
   BAR_C2DONE = 54,  // [2] C2 warps finished piece j (count 4), index j % 2
   BAR_D1READ = 56,  // [2] C1 warps read D1(j) (count 8), index j % 2
@@ -372,7 +372,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
         commit_one(bar(BAR_S2DONE + (j & 1)));
       }
     }
-    commit_one(bar(BAR_DRAIN));  // drain this warp's tensor-core work (as the S1 issuer)
+    commit_one(bar(BAR_DRAIN));  // drain this warp's tensor-core work (as the S1 issuer does)
     if (lane == 0) mbar_drain_spin(bar(BAR_DRAIN), 0);
     __syncwarp();
   } else if (warp == 13) {
@@ -397,7 +397,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ring_tc05_kernel(const TcParams
         if (j == np - 1) commit_one(bar(BAR_D3DONE));
       }
     }
-    commit_one(bar(BAR_DRAIN + 1));  // drain this warp's tensor-core work (as the S1 issuer)
+    commit_one(bar(BAR_DRAIN + 1));  // drain this warp's tensor-core work (as the S1 issuer does)
     if (lane == 0) mbar_drain_spin(bar(BAR_DRAIN + 1), 0);
     __syncwarp();
   } else {

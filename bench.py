@@ -29,6 +29,8 @@ Extra objects on the line:
   c1_chain         1920->2880->1920 up/down layers at R8, T=1: per-layer time from stream
                    launches and from a CUDA graph, against dense fp16 (the launch share a
                    persistent multi-layer kernel could remove);
+  premerge         the optional G1.G2 pre-merge measured as two cuBLAS GEMMs next to the
+                   fused operator (c1/c2 at T = 8/32);
   cpu_baseline     the reference's CPU contraction at 1 thread and at all host threads.
 value = mean over the five cases of the mean value-leg time (the device timer on this part ticks
 in ~2 us steps, so single-call medians are quantised; means over the steps are not).
@@ -724,6 +726,49 @@ def _graph_of(fn, arg):
         return str(e).splitlines()[0][:200]
 
 
+def premerge_leg(dev, flush):
+    """The optional G1.G2 pre-merge (north_star (a); bounded by IMPLEMENTATION.md:25 in the
+    reference), measured instead of built: the merged core M[a,(i,j),(p,q),c] = sum_b
+    A[a,p,i,b] B[b,q,j,c], then y by two cuBLAS GEMMs, X[(k,t),(i,j)] M[(i,j),(a,p,q,c)] and, after
+    a permute, T12[(t,p,q),(k,a,c)] C[(k,a,c),r].  Cold device time per call next to the fused
+    operator on the c1/c2 shapes at T = 8 and 32, with both forms' relative Frobenius error
+    against the fp32 contraction."""
+    from kernel_task_b200 import prepare_optimized
+    from kernel_task_b200.spec import SPEC_C1, SPEC_C2, baseline_cores, baseline_x
+
+    out = {}
+    for spec in (SPEC_C1, SPEC_C2):
+        cores = baseline_cores(spec, seed=0, dtype=torch.float16, device=dev)
+        A, B, C = cores
+        (ni, nj, nk), (P, Q, Rr), R = spec.input_modes, spec.output_modes, spec.rank
+        M = torch.einsum("apib,bqjc->aijpqc", A.float(), B.float()).to(torch.float16)
+        Mmat = M.permute(1, 2, 0, 3, 4, 5).reshape(ni * nj, R * P * Q * R).contiguous()
+        Cmat = C.permute(2, 3, 0, 1).reshape(nk * R * R, Rr).contiguous()
+        fn = prepare_optimized(cores, spec)
+        for T in (8, 32):
+            x = baseline_x(spec, T, seed=0, dtype=torch.float16, device=dev)
+
+            def merged(x=x, T=T):
+                xk = x.view(T, ni, nj, nk).permute(3, 0, 1, 2).reshape(nk * T, ni * nj)
+                t12 = (xk @ Mmat).view(nk, T, R, P, Q, R)
+                lhs = t12.permute(1, 3, 4, 0, 2, 5).reshape(T * P * Q, nk * R * R)
+                return (lhs @ Cmat).view(T, P * Q * Rr)
+
+            ym, yf = merged().float(), fn(x).float()
+            ref = torch.einsum("tijk,apib,bqjc,crka->tpqr",
+                               x.float().view(T, ni, nj, nk), A.float(), B.float(),
+                               C.float()).reshape(T, -1)
+            out[f"r{R}_t{T}"] = {
+                "merged_us": round(statistics.mean(cold_device_us(lambda _v: merged(), None,
+                                                                  flush, 30, 3)), 2),
+                "fused_us": round(statistics.mean(cold_device_us(fn, x, flush, 30, 3)), 2),
+                "merged_rel_frob": round(float((ym - ref).norm() / ref.norm()), 6),
+                "fused_rel_frob": round(float((yf - ref).norm() / ref.norm()), 6),
+                "merged_core_bytes": M.numel() * 2,
+                "intermediate_bytes": nk * T * R * P * Q * R * 2}
+    return out
+
+
 def c1_chain_leg(dev, layers=16):
     """The reference's comparison point for a persistent multi-layer kernel: a chain of
     1920->2880 (up) and 2880->1920 (down) R8 fp16 layers at T=1 (kernel_work/stack,
@@ -854,6 +899,7 @@ def run_ours(args, rank, world, local_rank):
     chain = (decode_chain_leg(dev, args.chain_layers)
              if args.chain_layers > 0 and world == 1 else None)
     c1_chain = c1_chain_leg(dev) if world == 1 and args.chain_layers > 0 else None
+    premerge = premerge_leg(dev, flush) if world == 1 and not args.no_dense else None
     clk = clocks.stop()  # sampled from before the cold legs to the end of the chain legs
     keys = list(cases)
     med = max_over_ranks([statistics.median(cases[k]["cold"]) for k in keys], world)
@@ -964,6 +1010,8 @@ def run_ours(args, rank, world, local_rank):
         line["decode_chain"] = chain
     if c1_chain is not None:
         line["c1_chain"] = c1_chain
+    if premerge is not None:
+        line["premerge"] = premerge
     if ref_gpu is not None:
         line["reference_gpu"] = {m: {k: v for k, v in r.items() if k != "cases"}
                                  for m, r in ref_gpu.items() if isinstance(r, dict)}

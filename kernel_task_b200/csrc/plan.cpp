@@ -682,8 +682,9 @@ int resolve_tc_geom(const Plan& p, int64_t T, const tr_tiling* f, TcGeom* g) {
   return TR_OK;
 }
 
-// Split of the slab kernel's pieces for `cols` tile columns: CL CTAs per cluster and NC <= 5
-// clusters per column, by an estimate of the device time in microseconds:
+// Split of the slab kernel's pieces for `cols` tile columns: CL CTAs per cluster and NC clusters
+// per column (at most 5, or as many as fit one wave), by an estimate of the device time in
+// microseconds:
 //   waves x pieces per CTA x (NSL slab steps of about 1 us + 0.3 us), where a wave holds
 //   max_clusters[CL] clusters (clusters of 8 fill 120 SMs of 148, of 4 132, of 2 all), plus with
 //   NC > 1 the slot pass (2 us plus NC / CL of a tile's partial sums at 1.4 us per 69 KB) and
@@ -703,7 +704,13 @@ static void slab_split(const Plan& p, long long cols, int64_t rows, int* CL, int
   *NC = 1;
   for (int cl = 16; cl >= 1; cl /= 2) {
     if (cl > m.npieces || p.max_clusters[cl] < 1) continue;
-    const int nc_max = std::min(nc_cap, m.npieces / cl);
+    // beyond nc_cap only as many clusters as still fit one wave (few columns, small T: config 3
+    // at T = 1 and 8 measured 181 -> 161 us and 192 -> 174 us with 7 clusters of 2 against 3
+    // of 4)
+    const long long nc_wave = std::min<long long>(p.max_clusters[cl] / std::max(1LL, cols),
+                                                  p.num_sms / std::max(1LL, cols * cl));
+    const int nc_max = (int)std::min<long long>(std::max<long long>(nc_cap, nc_wave),
+                                                m.npieces / cl);
     for (int nc = 1; nc <= nc_max; ++nc) {
       const int NJ = cl * nc;
       const long long waves = (cols * nc + p.max_clusters[cl] - 1) / p.max_clusters[cl];
